@@ -1,0 +1,141 @@
+/*
+ * pe_b200_attn.h -- C ABI of the B200 (sm_100a) packed variable-length attention backend.
+ *
+ * Plain pointers and sizes only. Every tensor lives in device memory of the current CUDA
+ * device and is owned by the caller; the library never allocates, frees or synchronises.
+ * Calls are enqueued on the stream given; no host reads of cu_seqlens values happen, so a
+ * call can be captured in a CUDA graph.
+ *
+ * Status codes: 0 ok; < 0 a rejected argument (nothing enqueued); see pe_b200_status_string.
+ */
+#ifndef PE_B200_ATTN_H
+#define PE_B200_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PE_B200_ABI_VERSION 1
+
+enum {
+  PE_B200_OK = 0,
+  PE_B200_ERR_NULL = -1,          /* a required pointer is NULL */
+  PE_B200_ERR_SHAPE = -2,         /* heads / kv_heads / head_dim / token counts invalid */
+  PE_B200_ERR_STRIDE = -3,        /* a stride or base address breaks the 16-byte TMA rule */
+  PE_B200_ERR_WINDOW = -4,        /* window_left / window_right < -1 */
+  PE_B200_ERR_WORKSPACE = -5,     /* workspace missing or smaller than pe_b200_attn_workspace_size */
+  PE_B200_ERR_DEVICE = -6,        /* current device is not sm_100 */
+  PE_B200_ERR_CUDA = -7,          /* a CUDA runtime/driver call failed (launch, tensor map) */
+  PE_B200_ERR_UNSUPPORTED = -8,   /* head_dim or layout outside what the kernels implement */
+};
+
+/* Device-side error bits, readable from the first 8 bytes of the workspace after a call. */
+enum {
+  PE_B200_DEVERR_WAIT_TIMEOUT = 1,
+  PE_B200_DEVERR_SCHEDULE_OVERFLOW = 2,
+  PE_B200_DEVERR_BAD_SEGMENTS = 4,
+};
+
+/*
+ * One packed attention call.
+ *
+ * q   [total_q, heads,    head_dim] bf16, element strides (q_stride_token, q_stride_head), D contiguous
+ * k,v [total_k, kv_heads, head_dim] bf16, likewise
+ * out [total_q, heads,    head_dim] bf16, likewise
+ * lse [heads, total_q] fp32 natural-log softmax denominator (optional, NULL to skip)
+ * cu_seqlens_q / cu_seqlens_k: int32 [n_seq + 1] device arrays, non-decreasing from 0.
+ *   For self attention pass the same pointer twice. When a query segment is shorter than
+ *   its key segment, the queries are the LAST rows of that key segment (end-aligned causal
+ *   mask), as in the reference's prefixed form.
+ * window_left / window_right: -1 unbounded, else the band (i - j) <= left, (j - i) <= right.
+ * causal: right context forced to 0.
+ * workspace: device memory of at least pe_b200_attn_workspace_size(...) bytes, 256-byte
+ *   aligned. It holds the tile schedule and the device error word; its contents are
+ *   rebuilt by every call, so one workspace serves calls on one stream in sequence.
+ *
+ * Replaces (packed-encoders 0.3.0):
+ *   packed_short_attention()      packed_encoders/_kernels/triton_packed_attention.py:175-236
+ *   flash_attn_varlen_func calls  packed_encoders/ops.py:432-461, :521-532
+ *   AttentionChoice.packed/.prefixed kernels
+ *                                 packed_encoders/runtime/attention.py:66-96, 104-126
+ *   pe_local_attention (CPU)      packed_encoders/cpu/local_attention_x86.c:192-235
+ */
+typedef struct PeB200AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  float* lse;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int32_t n_seq;
+  int32_t total_q;
+  int32_t total_k;
+  int32_t max_seqlen_q; /* host-known upper bound on any query segment length */
+  int32_t max_seqlen_k; /* host-known upper bound on any key segment length */
+  int32_t heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int64_t q_stride_token, q_stride_head;
+  int64_t k_stride_token, k_stride_head;
+  int64_t v_stride_token, v_stride_head;
+  int64_t o_stride_token, o_stride_head;
+  float scale;
+  int32_t window_left;
+  int32_t window_right;
+  int32_t causal;
+  void* workspace;
+  size_t workspace_bytes;
+} PeB200AttnParams;
+
+/* ABI version of the loaded library (PE_B200_ABI_VERSION). */
+int pe_b200_abi_version(void);
+
+/* Human-readable text for a status code. */
+const char* pe_b200_status_string(int status);
+
+/* 1 if `device` is an sm_100 part this library runs on, else 0. */
+int pe_b200_device_supported(int device);
+
+/*
+ * Bytes of workspace a call with these shapes needs (n_seq, total_q, max_seqlen_q,
+ * max_seqlen_k, head_dim are read; pointers are not). Returns a status code.
+ * Replaces the scratch sizing of CPUAttention._native_args, cpu/attention.py:418-430.
+ */
+int pe_b200_attn_workspace_size(const PeB200AttnParams* p, size_t* bytes);
+
+/*
+ * Enqueue packed attention on `stream` (a cudaStream_t; NULL = legacy default stream):
+ * the device tile-schedule builder, then the persistent tcgen05 attention kernel.
+ */
+int pe_b200_attn_fwd(const PeB200AttnParams* p, void* stream);
+
+/*
+ * Enqueue only the device tile-schedule builder into `p->workspace` (the first half of
+ * pe_b200_attn_fwd). Exposed for tests and for callers that reuse one schedule.
+ * Replaces the host-side sequence/tile bookkeeping of triton_packed_attention.py:212-215.
+ */
+int pe_b200_build_schedule(const PeB200AttnParams* p, void* stream);
+
+/* Enqueue the attention kernel on an already built schedule in `p->workspace`. */
+int pe_b200_attn_run(const PeB200AttnParams* p, void* stream);
+
+/*
+ * Debug / layout probes (one CTA, no schedule): QK^T of one 128-row query tile against one
+ * key tile into fp32 s_out [128, block_n]; and P.V with fp32 p_in [128, block_n] rounded to
+ * bf16 through TMEM into fp32 o_out [128, head_dim]. Rows/keys past the given counts are
+ * read as zero. Used by tests to pin the tcgen05 operand layouts.
+ */
+int pe_b200_debug_qk(const void* q, const void* k, int64_t q_stride_token, int64_t k_stride_token, int rows_q,
+                     int rows_k, int head_dim, float* s_out, void* stream);
+int pe_b200_debug_pv(const float* p_in, const void* v, int64_t v_stride_token, int rows_k, int head_dim,
+                     float* o_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PE_B200_ATTN_H */

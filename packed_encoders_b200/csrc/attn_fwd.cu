@@ -1,0 +1,951 @@
+// Packed variable-length attention for B200 (sm_100a): a device tile-schedule builder and a
+// persistent, warp-specialised tcgen05 forward kernel, behind the C ABI of pe_b200_attn.h.
+//
+// Work decomposition (packed_encoders/_kernels/triton_packed_attention.py:72-143 computes the
+// same function with one program per (sequence, head, 16/64-row query block)):
+//   * a WORK ITEM is one 128-row query tile. Sequences longer than 128 tokens get one item per
+//     128-row block; runs of consecutive short sequences (query and key spans <= 128 each) are
+//     packed greedily into ONE item whose key tile is block-diagonal: each row reads only the
+//     keys of its own sequence (the short-sequence variant);
+//   * items are ordered by cost (number of key tiles), longest first, and a UNIT is
+//     (item, head). CTA b of the persistent grid takes units b, b + grid, b + 2*grid, ...
+//   * per unit the key range is the union of the rows' allowed keys (window / causal), walked
+//     in key tiles of BN tokens; rows mask keys outside their own band.
+//
+// Roles inside one CTA (192 threads):
+//   warp 0        TMA producer: Q tile (double-buffered across units), K/V key tiles (ring)
+//   warp 1        MMA issuer: S = Q K^T (SS form) into a double-buffered TMEM S, then
+//                 O += P V with P read from TMEM (TS form); TMEM allocator
+//   warps 2..5    softmax + epilogue: one query row per thread (TMEM lane), exp2 online
+//                 softmax with fp32 row max / sum, bf16 P written back over S, O rescaled in
+//                 TMEM only when the running max grows by more than 2^8, final O / l -> bf16
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/pe_b200_attn.h"
+#include "sm100_ptx.cuh"
+
+namespace pe_b200 {
+
+constexpr int kTileM = 128;               // query rows per item / TMEM lanes
+constexpr int kHeaderBytes = 256;         // workspace header: n_items, error word
+constexpr int kCostBuckets = 1024;        // LPT ordering buckets (cost clamped)
+constexpr int kBuilderThreads = 1024;
+constexpr float kRescaleThreshold = 8.0f; // log2 units: rescale O only when the max grows > 2^8
+
+struct WorkItem {
+  int seq_first;  // first sequence of the item
+  int seq_count;  // 1 for a block of one sequence; >= 1 for a packed run of short sequences
+  int q_block;    // 128-row block index inside seq_first (0 for packed runs)
+  int cost;       // key tiles
+};
+
+struct WsHeader {
+  int n_items;
+  int error;
+};
+
+struct SchedParams {
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int n_seq;
+  int total_q;
+  int total_k;
+  int window_left;   // -1 unbounded
+  int window_right;  // -1 unbounded; 0 when causal
+  int block_n;       // key tile
+  int capacity;      // items the workspace holds
+  WsHeader* header;
+  WorkItem* items;
+};
+
+struct AttnParams {
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int heads;
+  int group;  // heads / kv_heads
+  int total_q;
+  __nv_bfloat16* out;
+  long long o_tok;
+  long long o_head;
+  float* lse;
+  float scale_log2;
+  int window_left;
+  int window_right;
+  const WsHeader* header;
+  const WorkItem* items;
+  int* err;
+};
+
+// ---------------------------------------------------------------------------------------------
+// Key range of a block of one sequence (shared by the builder's cost and the kernel's walk).
+// Query rows [qb*128, qb*128 + nq) of a segment with lq queries and lk keys; queries sit at key
+// position row + (lk - lq) (end-aligned). Returns [lo, hi) in key-local positions.
+__host__ __device__ __forceinline__ void block_key_range(int qb, int nq, int lq, int lk, int wl, int wr, int& lo,
+                                                         int& hi) {
+  int shift = lk - lq;
+  int p0 = qb * kTileM + shift;
+  int p1 = qb * kTileM + nq - 1 + shift;
+  lo = wl >= 0 ? max(0, p0 - wl) : 0;
+  hi = wr >= 0 ? min(lk, p1 + wr + 1) : lk;
+  if (hi < lo) hi = lo;
+}
+
+__device__ __forceinline__ int cost_bucket(int cost) { return min(max(cost, 0), kCostBuckets - 1); }
+
+// Greedy walk over sequences [lo, hi): emits items in order through `emit(WorkItem)`.
+template <class Emit>
+__device__ void walk_sequences(const SchedParams& p, int lo, int hi, Emit emit) {
+  int first = -1, count = 0, span_q = 0, span_k = 0;
+  auto close = [&]() {
+    if (first >= 0 && span_q > 0) {
+      WorkItem it{first, count, 0, (span_k + p.block_n - 1) / p.block_n};
+      emit(it);
+    }
+    first = -1;
+    count = 0;
+    span_q = span_k = 0;
+  };
+  for (int s = lo; s < hi; ++s) {
+    int lq = p.cu_q[s + 1] - p.cu_q[s];
+    int lk = p.cu_k[s + 1] - p.cu_k[s];
+    if (lq <= 0) {  // no query rows: keep contiguity of an open run if its keys fit
+      if (first >= 0 && span_k + lk <= kTileM) {
+        ++count;
+        span_k += lk;
+      } else {
+        close();
+      }
+      continue;
+    }
+    if (lq > kTileM || lk > kTileM) {  // a long sequence: one item per 128-row query block
+      close();
+      int nblk = (lq + kTileM - 1) / kTileM;
+      for (int qb = 0; qb < nblk; ++qb) {
+        int nq = min(kTileM, lq - qb * kTileM);
+        int klo, khi;
+        block_key_range(qb, nq, lq, lk, p.window_left, p.window_right, klo, khi);
+        WorkItem it{s, 1, qb, (khi - klo + p.block_n - 1) / p.block_n};
+        emit(it);
+      }
+      continue;
+    }
+    if (first >= 0 && span_q + lq <= kTileM && span_k + lk <= kTileM) {
+      ++count;
+      span_q += lq;
+      span_k += lk;
+    } else {
+      close();
+      first = s;
+      count = 1;
+      span_q = lq;
+      span_k = lk;
+    }
+  }
+  close();
+}
+
+__device__ int block_exclusive_scan(int v, int* tmp, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) tmp[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int s = lane < nw ? tmp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    tmp[lane] = s;
+  }
+  __syncthreads();
+  int off = (w > 0 ? tmp[w - 1] : 0) + x - v;
+  *total = tmp[nw - 1];
+  __syncthreads();
+  return off;
+}
+
+// One CTA builds the whole schedule: validate segments, greedy-pack per thread chunk, count
+// items per cost bucket, order buckets longest-first, scatter.
+__global__ void __launch_bounds__(kBuilderThreads) schedule_kernel(SchedParams p) {
+  __shared__ int hist[kCostBuckets];
+  __shared__ int cursor[kCostBuckets];
+  __shared__ int tmp[32];
+  __shared__ int bad;
+  const int tid = threadIdx.x;
+  for (int b = tid; b < kCostBuckets; b += blockDim.x) hist[b] = 0;
+  if (tid == 0) bad = 0;
+  __syncthreads();
+  for (int s = tid; s < p.n_seq; s += blockDim.x) {
+    int q0 = p.cu_q[s], q1 = p.cu_q[s + 1], k0 = p.cu_k[s], k1 = p.cu_k[s + 1];
+    bool ok = q0 <= q1 && k0 <= k1 && (q1 - q0) <= (k1 - k0) && q0 >= 0 && k0 >= 0 && q1 <= p.total_q &&
+              k1 <= p.total_k;
+    if (s == 0) ok = ok && q0 == 0 && k0 == 0;
+    if (s == p.n_seq - 1) ok = ok && q1 == p.total_q && k1 == p.total_k;
+    if (!ok) atomicOr(&bad, 1);
+  }
+  __syncthreads();
+  if (bad) {
+    if (tid == 0) {
+      p.header->n_items = 0;
+      atomicOr(&p.header->error, kErrBadSegments);
+    }
+    return;
+  }
+  const int chunk = (p.n_seq + blockDim.x - 1) / blockDim.x;
+  const int lo = min(p.n_seq, tid * chunk), hi = min(p.n_seq, lo + chunk);
+  walk_sequences(p, lo, hi, [&](const WorkItem& it) { atomicAdd(&hist[cost_bucket(it.cost)], 1); });
+  __syncthreads();
+  int total = 0;
+  for (int base = 0; base < kCostBuckets; base += blockDim.x) {  // blockDim == kCostBuckets
+    int b = kCostBuckets - 1 - (base + tid);
+    int off = block_exclusive_scan(b >= 0 ? hist[b] : 0, tmp, &total);
+    if (b >= 0) cursor[b] = off;
+  }
+  __syncthreads();
+  walk_sequences(p, lo, hi, [&](const WorkItem& it) {
+    int pos = atomicAdd(&cursor[cost_bucket(it.cost)], 1);
+    if (pos < p.capacity) p.items[pos] = it;
+  });
+  if (tid == 0) {
+    if (total > p.capacity) atomicOr(&p.header->error, kErrScheduleOverflow);
+    p.header->n_items = min(total, p.capacity);
+  }
+}
+
+__global__ void clear_header_kernel(WsHeader* h) {
+  h->n_items = 0;
+  h->error = 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Attention kernel configuration.
+template <int D_, int BN_, int ST_, int QB_>
+struct Cfg {
+  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_;
+  static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
+  static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
+  static constexpr int kKVPanelBytes = BN * 128;
+  static constexpr int kQBytes = kPanels * kQPanelBytes;
+  static constexpr int kKVBytes = kPanels * kKVPanelBytes;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + QB * kQBytes;
+  static constexpr int kOffV = kOffK + ST * kKVBytes;
+  static constexpr int kOffBar = kOffV + ST * kKVBytes;
+  // barriers: k_full[ST] v_full[ST] kv_empty[ST] q_full[QB] q_empty[QB] s_full[2] p_full[2] pv_done
+  static constexpr int kNumBars = 3 * ST + 2 * QB + 2 + 2 + 1;
+  static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColS0 = 0, kColS1 = BN, kColO = 256;
+  static_assert(2 * BN <= 256 && D <= 256, "TMEM budget");
+  static_assert(BN % 32 == 0 && D % 64 == 0, "tile shape");
+};
+
+struct UnitInfo {
+  int head, kv_head;
+  int f, c, qb;
+  int q_row0, nq;
+  int kv_lo, n_kv;
+};
+
+template <int BN>
+__device__ __forceinline__ UnitInfo unit_info(const AttnParams& p, long long u) {
+  UnitInfo ui;
+  const WorkItem it = p.items[u / p.heads];
+  ui.head = (int)(u % p.heads);
+  ui.kv_head = ui.head / p.group;
+  ui.f = it.seq_first;
+  ui.c = it.seq_count;
+  ui.qb = it.q_block;
+  const int cq0 = p.cu_q[ui.f], cqe = p.cu_q[ui.f + ui.c];
+  ui.q_row0 = cq0 + ui.qb * kTileM;
+  ui.nq = min(kTileM, cqe - ui.q_row0);
+  int kv_lo, kv_hi;
+  if (ui.c == 1) {
+    const int ck0 = p.cu_k[ui.f];
+    int lo, hi;
+    block_key_range(ui.qb, ui.nq, cqe - cq0, p.cu_k[ui.f + 1] - ck0, p.window_left, p.window_right, lo, hi);
+    kv_lo = ck0 + lo;
+    kv_hi = ck0 + hi;
+  } else {
+    kv_lo = p.cu_k[ui.f];
+    kv_hi = p.cu_k[ui.f + ui.c];
+  }
+  ui.kv_lo = kv_lo;
+  ui.n_kv = (ui.nq > 0 && kv_hi > kv_lo) ? (kv_hi - kv_lo + BN - 1) / BN : 0;
+  return ui;
+}
+
+template <class C>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* k_full = bars;
+  uint64_t* v_full = k_full + C::ST;
+  uint64_t* kv_empty = v_full + C::ST;
+  uint64_t* q_full = kv_empty + C::ST;
+  uint64_t* q_empty = q_full + C::QB;
+  uint64_t* s_full = q_empty + C::QB;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::ST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < C::QB; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
+    mbar_init(pv_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tm_q);
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const long long n_units = (long long)p.header->n_items * p.heads;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      long long i = 0;
+      int lu = 0;
+      for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const UnitInfo ui = unit_info<C::BN>(p, u);
+        if (ui.n_kv == 0) continue;
+        const int qb = lu % C::QB;
+        if (lu >= C::QB) mbar_wait(&q_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
+        uint8_t* qs = smem + C::kOffQ + qb * C::kQBytes;
+        mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
+#pragma unroll
+        for (int pn = 0; pn < C::kPanels; ++pn)
+          tma_load_3d(qs + pn * C::kQPanelBytes, &tm_q, &q_full[qb], pn * 64, ui.head, ui.q_row0);
+        for (int t = 0; t < ui.n_kv; ++t, ++i) {
+          const int st = (int)(i % C::ST);
+          if (i >= C::ST) mbar_wait(&kv_empty[st], (int)((i / C::ST) - 1) & 1, p.err);
+          const int row = ui.kv_lo + t * C::BN;
+          uint8_t* ks = smem + C::kOffK + st * C::kKVBytes;
+          uint8_t* vs = smem + C::kOffV + st * C::kKVBytes;
+          mbar_arrive_expect_tx(&k_full[st], C::kKVBytes);
+#pragma unroll
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_3d(ks + pn * C::kKVPanelBytes, &tm_k, &k_full[st], pn * 64, ui.kv_head, row);
+          mbar_arrive_expect_tx(&v_full[st], C::kKVBytes);
+#pragma unroll
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_3d(vs + pn * C::kKVPanelBytes, &tm_v, &v_full[st], pn * 64, ui.kv_head, row);
+        }
+        ++lu;
+      }
+      // Tail: every commit that targets this CTA's barriers has landed before exit.
+      for (long long j = (i > C::ST ? i - C::ST : 0); j < i; ++j)
+        mbar_wait(&kv_empty[j % C::ST], (int)(j / C::ST) & 1, p.err);
+      for (int j = (lu > C::QB ? lu - C::QB : 0); j < lu; ++j) mbar_wait(&q_empty[j % C::QB], (j / C::QB) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileM, C::BN, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(kTileM, C::D, false, true);
+      const uint32_t smem_base = smem_u32(smem);
+      long long i = 0;
+      int lu = 0;
+      long long prev_i = -1;
+      int prev_first = 0;
+      auto issue_pv = [&](long long j, int first) {
+        const int sb = (int)(j & 1);
+        const int st = (int)(j % C::ST);
+        mbar_wait(&p_full[sb], (int)(j >> 1) & 1, p.err);
+        mbar_wait(&v_full[st], (int)(j / C::ST) & 1, p.err);
+        tc_fence_after();
+        const uint32_t s_col = sb ? C::kColS1 : C::kColS0;
+        const uint32_t v_addr = smem_base + C::kOffV + st * C::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk) {
+          const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
+          mma_ts(tmem + C::kColO, tmem + s_col + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
+        }
+        mma_commit(pv_done);
+        mma_commit(&kv_empty[st]);
+      };
+      for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const UnitInfo ui = unit_info<C::BN>(p, u);
+        if (ui.n_kv == 0) continue;
+        const int qb = lu % C::QB;
+        mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
+        tc_fence_after();
+        const uint32_t q_addr = smem_base + C::kOffQ + qb * C::kQBytes;
+        for (int t = 0; t < ui.n_kv; ++t, ++i) {
+          const int st = (int)(i % C::ST);
+          const int sb = (int)(i & 1);
+          mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
+          tc_fence_after();
+          const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
+          const uint32_t s_col = sb ? C::kColS1 : C::kColS0;
+#pragma unroll
+          for (int kk = 0; kk < C::D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 0 + (kk & 3) * 32;
+            const uint64_t adesc = sw128_desc(q_addr + (kk >> 2) * C::kQPanelBytes + off, 16, 1024);
+            const uint64_t bdesc = sw128_desc(k_addr + (kk >> 2) * C::kKVPanelBytes + off, 16, 1024);
+            mma_ss(tmem + s_col, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[sb]);
+          if (t == ui.n_kv - 1) mma_commit(&q_empty[qb]);
+          if (prev_i >= 0) issue_pv(prev_i, prev_first);
+          prev_i = i;
+          prev_first = (t == 0);
+        }
+        ++lu;
+      }
+      if (prev_i >= 0) issue_pv(prev_i, prev_first);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row of this thread == TMEM lane
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    long long i = 0;
+    for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const UnitInfo ui = unit_info<C::BN>(p, u);
+      if (ui.n_kv == 0) continue;
+      // Allowed keys [klo, khi) of this row, in absolute key tokens.
+      const bool row_valid = r < ui.nq;
+      const int tq = ui.q_row0 + r;
+      int klo = 0, khi = 0;
+      if (row_valid) {
+        int s = ui.f;
+        if (ui.c > 1) {  // largest s in [f, f + c) with cu_q[s] <= tq
+          int a = ui.f, b = ui.f + ui.c - 1;
+          while (a < b) {
+            int mid = (a + b + 1) >> 1;
+            if (p.cu_q[mid] <= tq) a = mid; else b = mid - 1;
+          }
+          s = a;
+        }
+        const int cq = p.cu_q[s], lq = p.cu_q[s + 1] - cq;
+        const int ck = p.cu_k[s], lk = p.cu_k[s + 1] - ck;
+        const int pos = tq - cq + (lk - lq);
+        klo = ck + (p.window_left >= 0 ? max(0, pos - p.window_left) : 0);
+        khi = ck + (p.window_right >= 0 ? min(lk, pos + p.window_right + 1) : lk);
+      }
+      float m_run = NEG_INF, l_run = 0.f;
+      for (int t = 0; t < ui.n_kv; ++t, ++i) {
+        const int sb = (int)(i & 1);
+        const uint32_t s_col = sb ? C::kColS1 : C::kColS0;
+        const int kt = ui.kv_lo + t * C::BN;
+        mbar_wait(&s_full[sb], (int)(i >> 1) & 1, p.err);
+        tc_fence_after();
+        float x[C::BN];
+#pragma unroll
+        for (int cc = 0; cc < C::BN / 32; ++cc) {
+          uint32_t raw[32];
+          tmem_ld32(tmem + lane_base + s_col + cc * 32, raw);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) x[cc * 32 + j] = __uint_as_float(raw[j]);
+        }
+        float mx = NEG_INF;
+        const int c_lo = klo - kt, c_hi = khi - kt;  // valid columns [c_lo, c_hi)
+#pragma unroll
+        for (int j = 0; j < C::BN; ++j) {
+          const bool ok = j >= c_lo && j < c_hi;
+          x[j] = ok ? x[j] * p.scale_log2 : NEG_INF;
+          mx = fmaxf(mx, x[j]);
+        }
+        const float m_new = fmaxf(m_run, mx);
+        const bool need = (m_run != NEG_INF) && (m_new > m_run + kRescaleThreshold);
+        if (__any_sync(0xffffffffu, need)) {
+          // O holds the sum up to the previous key tile: wait for that P.V to land.
+          mbar_wait(pv_done, (int)((i - 1) & 1), p.err);
+          tc_fence_after();
+          const float alpha = need ? ex2(m_run - m_new) : 1.f;
+#pragma unroll
+          for (int cc = 0; cc < C::D / 32; ++cc) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_base + C::kColO + cc * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+            tmem_st32(tmem + lane_base + C::kColO + cc * 32, o);
+          }
+          tmem_wait_st();
+          l_run *= alpha;
+        }
+        if (m_run == NEG_INF || need) m_run = m_new;
+        const float base = (m_run == NEG_INF) ? 0.f : m_run;
+        float sum = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < C::BN / 32; ++cc) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float p0 = ex2(x[cc * 32 + 2 * j] - base);
+            const float p1 = ex2(x[cc * 32 + 2 * j + 1] - base);
+            sum += p0 + p1;
+            pk[j] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(tmem + lane_base + s_col + cc * 16, pk);
+        }
+        l_run += sum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[sb]);
+      }
+      // Epilogue: O / l -> bf16 rows, LSE in natural log.
+      mbar_wait(pv_done, (int)((i - 1) & 1), p.err);
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const bool store = row_valid && tq >= 0 && tq < p.total_q;
+      __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head;
+#pragma unroll
+      for (int cc = 0; cc < C::D / 32; ++cc) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + C::kColO + cc * 32, o);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        }
+      }
+      if (store && p.lse != nullptr) {
+        const float lse = l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : NEG_INF;
+        p.lse[(long long)ui.head * p.total_q + tq] = lse;
+      }
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Layout probes: one CTA of 128 threads runs a single QK^T or P.V through the same descriptor
+// code as the kernel above.
+template <int D>
+__global__ void __launch_bounds__(128, 1)
+    debug_qk_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, float* s_out,
+                    int* err) {
+  constexpr int BN = 128;
+  constexpr int kPanels = D / 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = smem;
+  uint8_t* ks = smem + kPanels * kTileM * 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ks + kPanels * BN * 128);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bars + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bars[0], kPanels * (kTileM + BN) * 128);
+    for (int pn = 0; pn < kPanels; ++pn) {
+      tma_load_3d(qs + pn * kTileM * 128, &tm_q, &bars[0], pn * 64, 0, 0);
+      tma_load_3d(ks + pn * BN * 128, &tm_k, &bars[0], pn * 64, 0, 0);
+    }
+    mbar_wait(&bars[0], 0, err);
+    tc_fence_after();
+    constexpr uint32_t idesc = idesc_bf16_f32(kTileM, BN, false, false);
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint32_t off = (kk & 3) * 32;
+      mma_ss(tmem, sw128_desc(smem_u32(qs) + (kk >> 2) * kTileM * 128 + off, 16, 1024),
+             sw128_desc(smem_u32(ks) + (kk >> 2) * BN * 128 + off, 16, 1024), idesc, kk > 0);
+    }
+    mma_commit(&bars[1]);
+  }
+  __syncwarp();
+  mbar_wait(&bars[1], 0, err);
+  tc_fence_after();
+  const int r = warp * 32 + lane;
+  for (int cc = 0; cc < BN / 32; ++cc) {
+    uint32_t raw[32];
+    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cc * 32, raw);
+    tmem_wait_ld();
+    for (int j = 0; j < 32; ++j) s_out[r * BN + cc * 32 + j] = __uint_as_float(raw[j]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(128, 1)
+    debug_pv_kernel(const __grid_constant__ CUtensorMap tm_v, const float* p_in, float* o_out, int* err) {
+  constexpr int BN = 128;
+  constexpr int kPanels = D / 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* vs = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kPanels * BN * 128);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bars + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  const int r = warp * 32 + lane;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  for (int cc = 0; cc < BN / 32; ++cc) {  // P row r -> bf16 pairs in TMEM columns [0, BN/2)
+    uint32_t pk[16];
+    for (int j = 0; j < 16; ++j)
+      pk[j] = pack_bf16x2(p_in[r * BN + cc * 32 + 2 * j], p_in[r * BN + cc * 32 + 2 * j + 1]);
+    tmem_st16(tmem + lane_base + cc * 16, pk);
+  }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    tc_fence_after();
+    mbar_arrive_expect_tx(&bars[0], kPanels * BN * 128);
+    for (int pn = 0; pn < kPanels; ++pn) tma_load_3d(vs + pn * BN * 128, &tm_v, &bars[0], pn * 64, 0, 0);
+    mbar_wait(&bars[0], 0, err);
+    constexpr uint32_t idesc = idesc_bf16_f32(kTileM, D, false, true);
+    for (int kk = 0; kk < BN / 16; ++kk)
+      mma_ts(tmem + 256, tmem + kk * 8, sw128_desc(smem_u32(vs) + kk * 16 * 128, BN * 128, 1024), idesc, kk > 0);
+    mma_commit(&bars[1]);
+  }
+  __syncwarp();
+  mbar_wait(&bars[1], 0, err);
+  tc_fence_after();
+  for (int cc = 0; cc < D / 32; ++cc) {
+    uint32_t raw[32];
+    tmem_ld32(tmem + lane_base + 256 + cc * 32, raw);
+    tmem_wait_ld();
+    for (int j = 0; j < 32; ++j) o_out[r * D + cc * 32 + j] = __uint_as_float(raw[j]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host side.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// [tokens, heads, D] bf16 with element strides (token, head); box = 64 columns x 1 head x rows.
+static bool make_map(CUtensorMap* map, const void* base, long long tokens, int heads, int dim, long long tok_stride,
+                     long long head_stride, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)dim, (cuuint64_t)heads, (cuuint64_t)tokens};
+  cuuint64_t strides[2] = {(cuuint64_t)head_stride * 2, (cuuint64_t)tok_stride * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int supported = -1;
+};
+
+static DeviceInfo& device_info(int dev) {
+  static DeviceInfo infos[64];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceInfo& d = infos[dev & 63];
+  if (d.supported < 0) {
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    d.sms = sms;
+    d.supported = (major == 10 && minor == 0) ? 1 : 0;
+  }
+  return d;
+}
+
+static int block_n_for(int head_dim) { return head_dim == 256 ? 64 : 128; }
+
+static long long item_capacity(const PeB200AttnParams* p) {
+  return (long long)p->n_seq + (long long)p->total_q / kTileM + 2;
+}
+
+static size_t workspace_bytes_for(const PeB200AttnParams* p) {
+  return (size_t)kHeaderBytes + sizeof(WorkItem) * (size_t)item_capacity(p);
+}
+
+static int validate(const PeB200AttnParams* p, bool need_tensors) {
+  if (!p) return PE_B200_ERR_NULL;
+  if (p->n_seq < 0 || p->total_q < 0 || p->total_k < 0 || p->heads < 1 || p->kv_heads < 1 ||
+      p->heads % p->kv_heads != 0)
+    return PE_B200_ERR_SHAPE;
+  if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256) return PE_B200_ERR_UNSUPPORTED;
+  if (p->window_left < -1 || p->window_right < -1) return PE_B200_ERR_WINDOW;
+  if (p->total_q > 0 && p->total_k == 0) return PE_B200_ERR_SHAPE;
+  if (!need_tensors) return PE_B200_OK;
+  if (!p->cu_seqlens_q || !p->cu_seqlens_k || !p->workspace) return PE_B200_ERR_NULL;
+  if (p->total_q > 0 && (!p->q || !p->out)) return PE_B200_ERR_NULL;
+  if (p->total_k > 0 && (!p->k || !p->v)) return PE_B200_ERR_NULL;
+  auto aligned16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out)) return PE_B200_ERR_STRIDE;
+  const int64_t strides[8] = {p->q_stride_token, p->q_stride_head, p->k_stride_token, p->k_stride_head,
+                              p->v_stride_token, p->v_stride_head, p->o_stride_token, p->o_stride_head};
+  for (int64_t s : strides)
+    if (s <= 0 || (s * 2) % 16 != 0) return PE_B200_ERR_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(p->workspace) & 255) != 0) return PE_B200_ERR_WORKSPACE;
+  if (p->workspace_bytes < workspace_bytes_for(p)) return PE_B200_ERR_WORKSPACE;
+  return PE_B200_OK;
+}
+
+template <class C>
+static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int sms) {
+  CUtensorMap tq, tk, tv;
+  if (!make_map(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
+      !make_map(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
+      !make_map(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN))
+    return PE_B200_ERR_CUDA;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return PE_B200_ERR_CUDA;
+    attr_set[dev & 63] = true;
+  }
+  AttnParams ap;
+  ap.cu_q = p->cu_seqlens_q;
+  ap.cu_k = p->cu_seqlens_k;
+  ap.heads = p->heads;
+  ap.group = p->heads / p->kv_heads;
+  ap.total_q = p->total_q;
+  ap.out = static_cast<__nv_bfloat16*>(p->out);
+  ap.o_tok = p->o_stride_token;
+  ap.o_head = p->o_stride_head;
+  ap.lse = p->lse;
+  ap.scale_log2 = p->scale * 1.4426950408889634f;
+  ap.window_left = p->window_left;
+  ap.window_right = p->causal ? 0 : p->window_right;
+  ap.header = static_cast<const WsHeader*>(p->workspace);
+  ap.items = reinterpret_cast<const WorkItem*>(static_cast<const uint8_t*>(p->workspace) + kHeaderBytes);
+  ap.err = &static_cast<WsHeader*>(p->workspace)->error;
+  const long long units = item_capacity(p) * p->heads;
+  const int grid = (int)(units < sms ? units : sms);
+  attn_fwd_kernel<C><<<grid, 192, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
+  return cudaGetLastError() == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
+}
+
+}  // namespace pe_b200
+
+using namespace pe_b200;
+
+extern "C" {
+
+int pe_b200_abi_version(void) { return PE_B200_ABI_VERSION; }
+
+const char* pe_b200_status_string(int status) {
+  switch (status) {
+    case PE_B200_OK: return "ok";
+    case PE_B200_ERR_NULL: return "a required pointer is NULL";
+    case PE_B200_ERR_SHAPE: return "invalid heads / kv_heads / head_dim / token counts";
+    case PE_B200_ERR_STRIDE: return "stride or base address not 16-byte aligned (TMA requirement)";
+    case PE_B200_ERR_WINDOW: return "window_left / window_right must be >= -1";
+    case PE_B200_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case PE_B200_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case PE_B200_ERR_CUDA: return "a CUDA launch or tensor-map call failed";
+    case PE_B200_ERR_UNSUPPORTED: return "head_dim must be 64, 128 or 256";
+    default: return "unknown status";
+  }
+}
+
+int pe_b200_device_supported(int device) { return device_info(device).supported == 1 ? 1 : 0; }
+
+int pe_b200_attn_workspace_size(const PeB200AttnParams* p, size_t* bytes) {
+  int st = validate(p, false);
+  if (st != PE_B200_OK) return st;
+  if (!bytes) return PE_B200_ERR_NULL;
+  *bytes = workspace_bytes_for(p);
+  return PE_B200_OK;
+}
+
+int pe_b200_build_schedule(const PeB200AttnParams* p, void* stream) {
+  int st = validate(p, true);
+  if (st != PE_B200_OK) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PE_B200_ERR_CUDA;
+  if (device_info(dev).supported != 1) return PE_B200_ERR_DEVICE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  WsHeader* header = static_cast<WsHeader*>(p->workspace);
+  clear_header_kernel<<<1, 1, 0, s>>>(header);
+  if (p->n_seq > 0 && p->total_q > 0) {
+    SchedParams sp;
+    sp.cu_q = p->cu_seqlens_q;
+    sp.cu_k = p->cu_seqlens_k;
+    sp.n_seq = p->n_seq;
+    sp.total_q = p->total_q;
+    sp.total_k = p->total_k;
+    sp.window_left = p->window_left;
+    sp.window_right = p->causal ? 0 : p->window_right;
+    sp.block_n = block_n_for(p->head_dim);
+    sp.capacity = (int)item_capacity(p);
+    sp.header = header;
+    sp.items = reinterpret_cast<WorkItem*>(static_cast<uint8_t*>(p->workspace) + kHeaderBytes);
+    schedule_kernel<<<1, kBuilderThreads, 0, s>>>(sp);
+  }
+  return cudaGetLastError() == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
+}
+
+int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
+  int st = validate(p, true);
+  if (st != PE_B200_OK) return st;
+  if (p->n_seq == 0 || p->total_q == 0) return PE_B200_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PE_B200_ERR_CUDA;
+  const DeviceInfo& info = device_info(dev);
+  if (info.supported != 1) return PE_B200_ERR_DEVICE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (p->head_dim) {
+    case 64: return launch_attention<Cfg<64, 128, 3, 2>>(p, s, info.sms);
+    case 128: return launch_attention<Cfg<128, 128, 2, 2>>(p, s, info.sms);
+    case 256: return launch_attention<Cfg<256, 64, 2, 1>>(p, s, info.sms);
+    default: return PE_B200_ERR_UNSUPPORTED;
+  }
+}
+
+int pe_b200_attn_fwd(const PeB200AttnParams* p, void* stream) {
+  int st = pe_b200_build_schedule(p, stream);
+  if (st != PE_B200_OK) return st;
+  return pe_b200_attn_run(p, stream);
+}
+
+int pe_b200_debug_qk(const void* q, const void* k, int64_t q_stride_token, int64_t k_stride_token, int rows_q,
+                     int rows_k, int head_dim, float* s_out, void* stream) {
+  if (!q || !k || !s_out) return PE_B200_ERR_NULL;
+  if (rows_q < 1 || rows_k < 1) return PE_B200_ERR_SHAPE;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return PE_B200_ERR_UNSUPPORTED;
+  CUtensorMap tq, tk;
+  if (!make_map(&tq, q, rows_q, 1, head_dim, q_stride_token, head_dim, kTileM) ||
+      !make_map(&tk, k, rows_k, 1, head_dim, k_stride_token, head_dim, 128))
+    return PE_B200_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int smem = (head_dim / 64) * (kTileM + 128) * 128 + 64 + 1024;
+  int* err = nullptr;
+  switch (head_dim) {
+#define PE_QK(D)                                                                                         \
+  case D:                                                                                                \
+    cudaFuncSetAttribute(debug_qk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
+    debug_qk_kernel<D><<<1, 128, smem, s>>>(tq, tk, s_out, err);                                         \
+    break;
+    PE_QK(64)
+    PE_QK(128)
+    PE_QK(256)
+#undef PE_QK
+  }
+  return cudaGetLastError() == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
+}
+
+int pe_b200_debug_pv(const float* p_in, const void* v, int64_t v_stride_token, int rows_k, int head_dim,
+                     float* o_out, void* stream) {
+  if (!p_in || !v || !o_out) return PE_B200_ERR_NULL;
+  if (rows_k < 1) return PE_B200_ERR_SHAPE;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return PE_B200_ERR_UNSUPPORTED;
+  CUtensorMap tv;
+  if (!make_map(&tv, v, rows_k, 1, head_dim, v_stride_token, head_dim, 128)) return PE_B200_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int smem = (head_dim / 64) * 128 * 128 + 64 + 1024;
+  int* err = nullptr;
+  switch (head_dim) {
+#define PE_PV(D)                                                                                         \
+  case D:                                                                                                \
+    cudaFuncSetAttribute(debug_pv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);         \
+    debug_pv_kernel<D><<<1, 128, smem, s>>>(tv, p_in, o_out, err);                                       \
+    break;
+    PE_PV(64)
+    PE_PV(128)
+    PE_PV(256)
+#undef PE_PV
+  }
+  return cudaGetLastError() == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
+}
+
+}  // extern "C"

