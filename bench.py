@@ -1,0 +1,487 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 packed attention backend (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Headline workload (config 3 of the benchmark plan, the document batch): 512 documents per
+GPU, lengths log-normal (median 600, sigma 0.8) clipped to [64, 8192], 16 heads x 64, bf16
+q/k/v ~ N(0,1); ONE STEP = the attention of a 28-layer ModernBERT-large stack, global
+attention every 3rd layer (10 global) and a +-64 sliding window elsewhere (18 local).
+Metric: useful-pair TFLOP/s = 4 * allowed (query, key) pairs * H * D / time, summed over all
+ranks' sequences / the slowest rank's time (weak scaling: the global batch is N x 512
+documents, token-balanced over the ranks by LPT sequence partition, no collective on the
+hot path).
+
+``--impl reference`` times the reference's own CPU path for the same workload on the
+host's cores (a bounded sample of the documents per step): its x86 C kernel
+``pe_local_attention`` (packed_encoders/cpu/local_attention_x86.c, compiled from the
+reference tree into oracle/_ref) for local layers and its per-sequence fp32 SDPA policy
+for global layers longer than 128 tokens (packed_encoders/cpu/attention.py:400-403,
+442-457).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one attn_fwd_kernel launch (config 3 global
+# layer), from the ncu capture summarised in profiles/attn_fwd_config3.md; None until captured.
+NCU_TRAFFIC_GLOBAL = None
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def _peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", data["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"pe_b200_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.25)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+                float(parts[1])
+            except ValueError:
+                rows.pop()
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        loaded = [x for x in sm if x > 0.5 * max(sm)] or sm
+        names = {5: "hw_slowdown", 6: "hw_thermal_slowdown", 7: "sw_thermal_slowdown", 8: "sw_power_cap"}
+        reasons = sorted({names[i] for r in rows for i in names if r[i].lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace('.', '', 1).isdigit())
+                if any(r[3].replace('.', '', 1).isdigit() for r in rows) else None}
+
+
+# ----------------------------------------------------------------------------------------- CPU
+def cpu_reference_sample(lengths, heads, layers, *, threads, seed=5):
+    """Time the reference CPU path on `lengths` (one pass of `layers`). Returns (seconds, flops)."""
+    import torch.nn.functional as F
+
+    import oracle
+    from packed_encoders_b200.workloads import useful_flops
+
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(seed)
+    total = sum(lengths)
+    q, k, v = (torch.randn(1, heads, total, 64, generator=gen) for _ in range(3))
+    cu = [0]
+    for n in lengths:
+        cu.append(cu[-1] + n)
+    flops = 0
+    start = time.perf_counter()
+    with torch.inference_mode():
+        for window, causal in layers:
+            if window == (-1, -1) and max(lengths) > 128:
+                # CPUAttention.global_ -> _sdpa for sequences past 128 (cpu/attention.py:400-403,442-457)
+                for a, b in zip(cu, cu[1:]):
+                    F.scaled_dot_product_attention(q[:, :, a:b], k[:, :, a:b], v[:, :, a:b])
+            else:
+                half = max(lengths) if window == (-1, -1) else window[0]
+                oracle.reference_local_attention(q[0], k[0], v[0], lengths, half, threads=threads)
+            flops += useful_flops(lengths, heads, 64, window, causal)
+    return time.perf_counter() - start, flops
+
+
+def sample_lengths(lengths, every):
+    return [n for i, n in enumerate(lengths) if i % every == 0]
+
+
+# ----------------------------------------------------------------------------------------- GPU
+def make_step(pe, q, k, v, cu, max_len, layers, *, record_kernel=None):
+    """One step = the attention of every layer in `layers`: one tile schedule per attention
+    kind (built on device each step), then one kernel launch per layer. When `record` is a
+    list, CUDA events bracket each launch of kind `record_kernel` on the launching stream."""
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream()
+    scale = q.shape[2] ** -0.5
+
+    def one_step(record=None):
+        plans = {kind: pe.ops.plan_attention(q, k, cu, max_len, window=kind[0], causal=kind[1])
+                 for kind in sorted(set(layers))}
+        for window, causal in layers:
+            ev = None
+            if record is not None and (window, causal) == record_kernel:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record(stream)
+            pe.packed_attention(q, k, v, cu, max_len, scale=scale, window=window, causal=causal, out=out,
+                                plan=plans[(window, causal)])
+            if ev is not None:
+                ev[1].record(stream)
+                record.append(ev)
+        return out
+
+    return one_step, out
+
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    import packed_encoders_b200 as pe
+    from packed_encoders_b200 import shard as shard_mod
+    from packed_encoders_b200 import workloads as wl
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local_rank = _env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    layers = wl.config3("mix").layers
+    lengths_all = wl.config3_lengths(512 * world, seed=0)
+    costs = [shard_mod.pattern_cost(n, (wl.GLOBAL, wl.LOCAL64), alpha=64.0) for n in lengths_all]
+    shards = shard_mod.partition(lengths_all, world, costs)
+    my = shards[rank]
+    heads, dim = 16, 64
+    q, k, v = wl.make_qkv(my.lengths, heads, heads, dim, seed=1 + rank, device=device)
+    cu = my.cu_seqlens(device)
+    max_len = max(my.lengths)
+    flops_by_kind = {kind: wl.useful_flops(my.lengths, heads, dim, *kind) for kind in set(layers)}
+    step_flops = sum(flops_by_kind[kind] for kind in layers)
+
+    one_step, out = make_step(pe, q, k, v, cu, max_len, layers, record_kernel=wl.GLOBAL)
+    for _ in range(args.warmup):
+        one_step(None)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    launches0 = pe.ops.LAUNCHES["kernels"]
+    kernel_events = []
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            one_step(kernel_events)
+        end.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    launches = pe.ops.LAUNCHES["kernels"] - launches0
+    elapsed_ms = start.elapsed_time(end)
+    kernel_ms = [a.elapsed_time(b) for a, b in kernel_events]
+    err = pe.device_error_word()
+
+    # e2e: the same step through the public API from pinned host buffers, H2D + D2H timed.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hcu = cu.cpu().pin_memory()
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hcu))
+    d2h = hout.numel() * hout.element_size()
+    e2e_steps = max(1, min(args.steps, 5))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        cu.copy_(hcu, non_blocking=True)
+        res = one_step(None)
+        hout.copy_(res, non_blocking=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    totals = torch.tensor([elapsed_ms, e2e_ms, float(step_flops), float(my.tokens), float(h2d), float(d2h)],
+                          dtype=torch.float64, device=device)
+    if world > 1:
+        tmax = totals[:2].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = totals[2:].clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        elapsed_ms, e2e_ms = tmax.tolist()
+        step_flops_all, tokens_all, h2d_all, d2h_all = tsum.tolist()
+    else:
+        step_flops_all, tokens_all, h2d_all, d2h_all = float(step_flops), float(my.tokens), float(h2d), float(d2h)
+
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    peaks = _peaks()
+    ms_per_step = elapsed_ms / args.steps
+    value = step_flops_all * args.steps / (elapsed_ms / 1e3) / 1e12
+    e2e_value = step_flops_all * e2e_steps / (e2e_ms / 1e3) / 1e12
+    avg_kernel_ms = statistics.mean(kernel_ms) if kernel_ms else None
+    achieved = flops_by_kind[wl.GLOBAL] / (avg_kernel_ms / 1e3) / 1e12 if avg_kernel_ms else None
+    traffic = None
+    if NCU_TRAFFIC_GLOBAL is not None:
+        traffic = NCU_TRAFFIC_GLOBAL
+    record = {
+        "metric": "useful-pair attention TFLOP/s, 28-layer ModernBERT-large document batch (10 global + 18 local)",
+        "value": round(value, 3),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": "config3-document-batch: 512 docs/GPU, lognormal(median 600, sigma 0.8) in [64,8192], "
+                        "16 heads x 64, 28 layers (global every 3rd, else window +-64)",
+            "heads": heads, "head_dim": dim, "n_seq_per_gpu": 512, "tokens_rank0": my.tokens,
+            "tokens_all_ranks": int(tokens_all), "global_batch_seqs": 512 * world,
+            "parallelism": f"dp{world} (LPT token-balanced sequence partition, no collective)",
+            "l2": "inputs larger than L2 (q,k,v,out = %.2f GB per layer)" % (
+                (q.numel() + k.numel() + v.numel() + out.numel()) * 2 / 1e9),
+        },
+        "tokens_per_s": round(tokens_all * args.steps / (elapsed_ms / 1e3), 1),
+        "roofline": {
+            "kernel": "attn_fwd_kernel (global layer, config 3)",
+            "bound": "tensor",
+            "achieved": round(achieved, 3) if achieved else None,
+            "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peaks["bf16_tflops"], 4) if achieved else None,
+            "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4) if achieved else None,
+            "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops burst)",
+            "traffic": traffic,
+            "avg_launch_ms": round(avg_kernel_ms, 4) if avg_kernel_ms else None,
+            "launches": len(kernel_ms),
+        },
+        "e2e": {
+            "value": round(e2e_value, 3), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": int(h2d_all), "d2h_bytes_per_step": int(d2h_all),
+            "steps": e2e_steps,
+            "note": "per step: pinned H2D of q,k,v,cu_seqlens, the 28-layer attention through "
+                    "packed_encoders_b200.packed_attention, D2H of the output",
+        },
+        "clocks": clocks.summary(),
+        "gpu_launches": launches,
+        "device_error_word": err,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        record["cpu_baseline"] = cpu_baseline_record(args)
+    if world == 1 and not args.no_extra:
+        record["workloads"] = extra_workloads(pe, wl, peaks)
+    print(json.dumps(record), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline_record(args, target_s=12.0):
+    from packed_encoders_b200 import workloads as wl
+
+    threads = max(1, len(os.sched_getaffinity(0)))
+    w = wl.config3("mix")
+    sample = sample_lengths(w.lengths, 32)
+    secs, flops, reps = 0.0, 0, 0
+    while secs < target_s and reps < 20:
+        s, f = cpu_reference_sample(sample, w.heads, w.layers, threads=threads)
+        secs += s
+        flops += f
+        reps += 1
+    return {"value": round(flops / secs / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+            "sample": f"every 32nd document of config 3 ({len(sample)} docs, {sum(sample)} tokens), 28-layer "
+                      f"pattern, {reps} passes, {secs:.1f} s; local: reference pe_local_attention (oracle/_ref), "
+                      f"global: reference per-sequence fp32 SDPA policy"}
+
+
+def extra_workloads(pe, wl, peaks, iters=10):
+    """Per-configuration single-launch numbers (L2 flushed between timed launches)."""
+    res = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    cases = [
+        ("config1-global", wl.config1("global")), ("config1-local", wl.config1("local")),
+        ("config2-query-batch", wl.config2()),
+        ("config3-global", wl.config3("global")), ("config3-local", wl.config3("local")),
+        ("config5-gqa-causal", wl.config5()),
+    ]
+    for name, w in cases:
+        q, k, v = wl.make_qkv(w.lengths, w.heads, w.kv_heads, w.head_dim, seed=1)
+        cu = w.cu_seqlens().cuda()
+        (window, causal), = set(w.layers)
+        out = torch.empty_like(q)
+        plan = pe.ops.plan_attention(q, k, cu, max(w.lengths), window=window, causal=causal)
+        times = []
+        for i in range(iters + 3):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            pe.packed_attention(q, k, v, cu, max(w.lengths), scale=w.scale, window=window, causal=causal,
+                                out=out, plan=plan)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= 3:
+                times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        flops = wl.useful_flops(w.lengths, w.heads, w.head_dim, window, causal)
+        nbytes = wl.algorithmic_bytes(w.tokens, w.tokens, w.heads, w.kv_heads, w.head_dim)
+        tflops = flops / (ms / 1e3) / 1e12
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"ms": round(ms, 4), "tflops": round(tflops, 2), "tokens_per_s": round(w.tokens / (ms / 1e3), 1),
+                     "hbm_gbs": round(gbs, 1), "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
+                     "hbm_frac": round(gbs / peaks["hbm_gbs"], 4), "tokens": w.tokens}
+        del q, k, v, out, plan
+    return res
+
+
+def run_reference(args):
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    if rank != 0:
+        return
+    from packed_encoders_b200 import workloads as wl
+
+    import oracle
+
+    if oracle.available_reference() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference CPU kernel (oracle/_ref) not built for this "
+                          "host's ISA"}))
+        return
+    threads = max(1, len(os.sched_getaffinity(0)))
+    w = wl.config3("mix")
+    sample = sample_lengths(w.lengths, 32)
+    for _ in range(args.warmup):
+        cpu_reference_sample(sample, w.heads, w.layers, threads=threads)
+    secs, flops = 0.0, 0
+    for _ in range(args.steps):
+        s, f = cpu_reference_sample(sample, w.heads, w.layers, threads=threads)
+        secs += s
+        flops += f
+    value = flops / secs / 1e12
+    record = {
+        "impl": "reference",
+        "metric": "useful-pair attention TFLOP/s, 28-layer ModernBERT-large document batch (10 global + 18 local)",
+        "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs / args.steps * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config3-document-batch (bounded sample: every 32nd document per step)",
+                   "heads": w.heads, "head_dim": 64, "sample_docs": len(sample), "sample_tokens": sum(sample)},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                         "sample": f"{len(sample)} of 512 documents per step"},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(record), flush=True)
+
+
+def run_case(args):
+    """Profiling helper: ``--case NAME --iters N [--seqs S]`` launches one configuration N times
+    (no timing output), e.g. for an ncu capture of a small case of the same kernel."""
+    import packed_encoders_b200 as pe
+    from packed_encoders_b200 import workloads as wl
+
+    makers = {"config1-global": lambda: wl.config1("global"), "config1-local": lambda: wl.config1("local"),
+              "config2": wl.config2, "config3-global": lambda: wl.config3("global"),
+              "config3-local": lambda: wl.config3("local"), "config5": wl.config5}
+    w = makers[args.case]()
+    lengths = list(w.lengths[: args.seqs]) if args.seqs else list(w.lengths)
+    q, k, v = wl.make_qkv(lengths, w.heads, w.kv_heads, w.head_dim, seed=1)
+    cu = torch.zeros(len(lengths) + 1, dtype=torch.int32)
+    cu[1:] = torch.tensor(lengths).cumsum(0)
+    cu = cu.cuda()
+    (window, causal), = set(w.layers)
+    out = torch.empty_like(q)
+    for _ in range(args.iters):
+        pe.packed_attention(q, k, v, cu, max(lengths), scale=w.scale, window=window, causal=causal, out=out)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, "tokens": sum(lengths), "seqs": len(lengths), "iters": args.iters,
+                      "device_error_word": pe.device_error_word()}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, help="profiling helper: run one configuration --iters times")
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--seqs", type=int, default=0, help="with --case: use only the first SEQS sequences")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

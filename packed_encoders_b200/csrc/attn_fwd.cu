@@ -754,7 +754,9 @@ static size_t workspace_bytes_for(const PeB200AttnParams* p) {
   return (size_t)kHeaderBytes + sizeof(WorkItem) * (size_t)item_capacity(p);
 }
 
-static int validate(const PeB200AttnParams* p, bool need_tensors) {
+enum ValidateLevel { kShapes = 0, kSchedule = 1, kFull = 2 };
+
+static int validate(const PeB200AttnParams* p, int level) {
   if (!p) return PE_B200_ERR_NULL;
   if (p->n_seq < 0 || p->total_q < 0 || p->total_k < 0 || p->heads < 1 || p->kv_heads < 1 ||
       p->heads % p->kv_heads != 0)
@@ -762,8 +764,11 @@ static int validate(const PeB200AttnParams* p, bool need_tensors) {
   if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256) return PE_B200_ERR_UNSUPPORTED;
   if (p->window_left < -1 || p->window_right < -1) return PE_B200_ERR_WINDOW;
   if (p->total_q > 0 && p->total_k == 0) return PE_B200_ERR_SHAPE;
-  if (!need_tensors) return PE_B200_OK;
+  if (level == kShapes) return PE_B200_OK;
   if (!p->cu_seqlens_q || !p->cu_seqlens_k || !p->workspace) return PE_B200_ERR_NULL;
+  if ((reinterpret_cast<uintptr_t>(p->workspace) & 255) != 0) return PE_B200_ERR_WORKSPACE;
+  if (p->workspace_bytes < workspace_bytes_for(p)) return PE_B200_ERR_WORKSPACE;
+  if (level == kSchedule) return PE_B200_OK;
   if (p->total_q > 0 && (!p->q || !p->out)) return PE_B200_ERR_NULL;
   if (p->total_k > 0 && (!p->k || !p->v)) return PE_B200_ERR_NULL;
   auto aligned16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
@@ -772,8 +777,6 @@ static int validate(const PeB200AttnParams* p, bool need_tensors) {
                               p->v_stride_token, p->v_stride_head, p->o_stride_token, p->o_stride_head};
   for (int64_t s : strides)
     if (s <= 0 || (s * 2) % 16 != 0) return PE_B200_ERR_STRIDE;
-  if ((reinterpret_cast<uintptr_t>(p->workspace) & 255) != 0) return PE_B200_ERR_WORKSPACE;
-  if (p->workspace_bytes < workspace_bytes_for(p)) return PE_B200_ERR_WORKSPACE;
   return PE_B200_OK;
 }
 
@@ -841,7 +844,7 @@ const char* pe_b200_status_string(int status) {
 int pe_b200_device_supported(int device) { return device_info(device).supported == 1 ? 1 : 0; }
 
 int pe_b200_attn_workspace_size(const PeB200AttnParams* p, size_t* bytes) {
-  int st = validate(p, false);
+  int st = validate(p, kShapes);
   if (st != PE_B200_OK) return st;
   if (!bytes) return PE_B200_ERR_NULL;
   *bytes = workspace_bytes_for(p);
@@ -849,7 +852,7 @@ int pe_b200_attn_workspace_size(const PeB200AttnParams* p, size_t* bytes) {
 }
 
 int pe_b200_build_schedule(const PeB200AttnParams* p, void* stream) {
-  int st = validate(p, true);
+  int st = validate(p, kSchedule);
   if (st != PE_B200_OK) return st;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return PE_B200_ERR_CUDA;
@@ -876,7 +879,7 @@ int pe_b200_build_schedule(const PeB200AttnParams* p, void* stream) {
 }
 
 int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
-  int st = validate(p, true);
+  int st = validate(p, kFull);
   if (st != PE_B200_OK) return st;
   if (p->n_seq == 0 || p->total_q == 0) return PE_B200_OK;
   int dev = 0;
@@ -893,7 +896,9 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
 }
 
 int pe_b200_attn_fwd(const PeB200AttnParams* p, void* stream) {
-  int st = pe_b200_build_schedule(p, stream);
+  int st = validate(p, kFull);
+  if (st != PE_B200_OK) return st;
+  st = pe_b200_build_schedule(p, stream);
   if (st != PE_B200_OK) return st;
   return pe_b200_attn_run(p, stream);
 }

@@ -74,6 +74,78 @@ class LaunchShape:
     max_seqlen_k: int
 
 
+LAUNCHES = {"kernels": 0}  # kernels enqueued by this module (bench / test bookkeeping)
+
+
+def _count(n: int) -> None:
+    LAUNCHES["kernels"] += n
+
+
+class AttentionPlan:
+    """A device tile schedule built once for one set of segment boundaries and one attention
+    kind (window / causal / head_dim), reusable by every layer of a forward that shares them
+    (e.g. all global layers of a packed ModernBERT forward). Building enqueues two small
+    kernels on the current stream and reads no device values on the host, so it can be
+    captured in a CUDA graph. Calls that use the plan must run on the same stream (or after
+    it) and must not overlap with a rebuild of it."""
+
+    def __init__(self, cu_seqlens: Tensor, max_seqlen: int, *, total_q: int, total_k: int | None = None,
+                 head_dim: int, window: tuple[int, int] = (-1, -1), causal: bool = False,
+                 cu_seqlens_k: Tensor | None = None, max_seqlen_k: int | None = None):
+        if head_dim not in SUPPORTED_HEAD_DIMS:
+            raise UnsupportedTargetError(f"b200 attention supports head_dim {SUPPORTED_HEAD_DIMS}, got {head_dim}")
+        self.cu_q = cu_seqlens
+        self.cu_k = cu_seqlens if cu_seqlens_k is None else cu_seqlens_k
+        self.max_q = int(max_seqlen)
+        self.max_k = int(max_seqlen if max_seqlen_k is None else max_seqlen_k)
+        self.total_q = int(total_q)
+        self.total_k = int(total_q if total_k is None else total_k)
+        self.head_dim = int(head_dim)
+        self.window = tuple(int(w) for w in window)
+        self.causal = bool(causal)
+        self.workspace: Tensor | None = None
+        self.build()
+
+    def key(self):
+        return (self.cu_q.data_ptr(), self.cu_k.data_ptr(), self.total_q, self.total_k, self.head_dim, self.window,
+                self.causal)
+
+    def _params(self) -> _lib.PeB200AttnParams:
+        return _lib.PeB200AttnParams(
+            cu_seqlens_q=_ptr(self.cu_q), cu_seqlens_k=_ptr(self.cu_k), n_seq=self.cu_q.numel() - 1,
+            total_q=self.total_q, total_k=self.total_k, max_seqlen_q=self.max_q, max_seqlen_k=self.max_k,
+            heads=1, kv_heads=1, head_dim=self.head_dim, window_left=self.window[0], window_right=self.window[1],
+            causal=int(self.causal), q_stride_token=8, q_stride_head=8, k_stride_token=8, k_stride_head=8,
+            v_stride_token=8, v_stride_head=8, o_stride_token=8, o_stride_head=8, scale=1.0)
+
+    def build(self) -> None:
+        params = self._params()
+        so = _lib.lib()
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(so.pe_b200_attn_workspace_size(ctypes.byref(params), ctypes.byref(nbytes)), "workspace size")
+        device = self.cu_q.device
+        if self.workspace is None or self.workspace.numel() < nbytes.value:
+            self.workspace = torch.empty(max(nbytes.value, 1 << 12), dtype=torch.uint8, device=device)
+        params.workspace = self.workspace.data_ptr()
+        params.workspace_bytes = self.workspace.numel()
+        with torch.cuda.device(device):
+            stream = torch.cuda.current_stream(device)
+            _lib.check(so.pe_b200_build_schedule(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)),
+                       "pe_b200_build_schedule")
+        _count(2)
+
+    def error_word(self) -> int:
+        """Synchronising read of the device error word of the last build / run on this plan."""
+        return int(self.workspace[4:8].view(torch.int32).item())
+
+
+def plan_attention(q: Tensor, k: Tensor, cu_seqlens: Tensor, max_seqlen: int, *, window=(-1, -1), causal=False,
+                   cu_seqlens_k: Tensor | None = None, max_seqlen_k: int | None = None) -> AttentionPlan:
+    """Build the tile schedule for ``packed_attention(q, k, v, cu_seqlens, ..., plan=...)``."""
+    return AttentionPlan(cu_seqlens, max_seqlen, total_q=q.shape[0], total_k=k.shape[0], head_dim=q.shape[2],
+                         window=window, causal=causal, cu_seqlens_k=cu_seqlens_k, max_seqlen_k=max_seqlen_k)
+
+
 def packed_attention(
     q: Tensor,
     k: Tensor,
@@ -88,6 +160,7 @@ def packed_attention(
     max_seqlen_k: int | None = None,
     out: Tensor | None = None,
     return_lse: bool = False,
+    plan: AttentionPlan | None = None,
 ):
     """Packed variable-length attention on B200.
 
@@ -97,6 +170,7 @@ def packed_attention(
     it (the reference's prefixed form, runtime/attention.py:242-261). ``window`` is
     ``(left, right)`` with -1 unbounded (runtime/attention.py:157-170). Returns ``out``
     ``[Tq, H, D]`` bf16, and with ``return_lse`` also the fp32 natural-log LSE ``[H, Tq]``.
+    ``plan`` (from ``plan_attention``) reuses an already built tile schedule.
     """
     _check_qkv(q, k, v)
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
@@ -141,14 +215,25 @@ def packed_attention(
         window_left=left, window_right=right, causal=int(bool(causal)),
     )
     so = _lib.lib()
-    nbytes = ctypes.c_size_t(0)
-    _lib.check(so.pe_b200_attn_workspace_size(ctypes.byref(params), ctypes.byref(nbytes)), "workspace size")
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device)
-        ws = _workspace(q.device, stream, nbytes.value)
-        params.workspace = ws.data_ptr()
-        params.workspace_bytes = ws.numel()
-        _lib.check(so.pe_b200_attn_fwd(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)), "pe_b200_attn_fwd")
+        if plan is not None:
+            if plan.key() != (cu_seqlens.data_ptr(), cu_k.data_ptr(), tq, tk, dim, (left, right), bool(causal)):
+                raise UnsupportedTargetError("plan was built for other segments / window / causal / head_dim")
+            params.workspace = plan.workspace.data_ptr()
+            params.workspace_bytes = plan.workspace.numel()
+            _lib.check(so.pe_b200_attn_run(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)),
+                       "pe_b200_attn_run")
+            _count(1)
+        else:
+            nbytes = ctypes.c_size_t(0)
+            _lib.check(so.pe_b200_attn_workspace_size(ctypes.byref(params), ctypes.byref(nbytes)), "workspace size")
+            ws = _workspace(q.device, stream, nbytes.value)
+            params.workspace = ws.data_ptr()
+            params.workspace_bytes = ws.numel()
+            _lib.check(so.pe_b200_attn_fwd(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)),
+                       "pe_b200_attn_fwd")
+            _count(3)
     return (out, lse) if return_lse else out
 
 
