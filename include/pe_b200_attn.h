@@ -30,6 +30,7 @@ enum {
   PE_B200_ERR_DEVICE = -6,        /* current device is not sm_100 */
   PE_B200_ERR_CUDA = -7,          /* a CUDA runtime/driver call failed (launch, tensor map) */
   PE_B200_ERR_UNSUPPORTED = -8,   /* head_dim or layout outside what the kernels implement */
+  PE_B200_ERR_SCRATCH_LIMIT = -9, /* call too large for pe_b200_attn_fwd_noalloc's fixed scratch */
 };
 
 /* Device-side error bits, readable from the first 8 bytes of the workspace after a call. */
@@ -122,6 +123,21 @@ int pe_b200_build_schedule(const PeB200AttnParams* p, void* stream);
 
 /* Enqueue the attention kernel on an already built schedule in `p->workspace`. */
 int pe_b200_attn_run(const PeB200AttnParams* p, void* stream);
+
+/*
+ * Same as pe_b200_attn_fwd, for callers that cannot give this library any device memory:
+ * a plugin whose host framework passes only a stream and the tensors, a binding from a
+ * language runtime without its own CUDA allocation calls, or a server that reserves all
+ * device memory at start-up and allows no allocation per request. p->workspace and
+ * p->workspace_bytes are ignored; the tile schedule and error word live in a fixed 1 MiB
+ * array inside the library's device memory (held on every GPU that loads the library until
+ * the process exits). Limit: n_seq + total_q / 128 + 2 <= 65,520, else
+ * PE_B200_ERR_SCRATCH_LIMIT and nothing is enqueued. The first call on a device looks up the
+ * array's address with that device current; make it before any stream capture. All calls
+ * share the array, so calls that overlap on the GPU race: serialise them. Nothing here
+ * allocates. This entry point has no counterpart in the reference.
+ */
+int pe_b200_attn_fwd_noalloc(const PeB200AttnParams* p, void* stream);
 
 /*
  * Debug / layout probes (one CTA, no schedule): QK^T of one 128-row query tile against one

@@ -18,7 +18,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libpe_b200.so"
-SOURCES = [CSRC / "attn_fwd.cu"]
+SOURCES = [CSRC / "attn_fwd.cu", CSRC / "noalloc.cu"]
 HEADERS = [ROOT / "include" / "pe_b200_attn.h", CSRC / "sm100_ptx.cuh"]
 
 NVCC_FLAGS = [
