@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -231,9 +232,13 @@ __global__ void clear_header_kernel(WsHeader* h) {
 
 // ---------------------------------------------------------------------------------------------
 // Attention kernel configuration.
-template <int D_, int BN_, int ST_, int QB_>
+//   D   head_dim;  BN key-tile rows;  ST K/V ring stages;  QB Q-tile buffers;
+//   NS  S buffers in TMEM (2: QK of the next key tile overlaps the softmax of this one;
+//       1: a single S, so two CTAs share an SM and overlap each other instead);
+//   CPS CTAs per SM the configuration is sized for (TMEM columns, shared memory, registers).
+template <int D_, int BN_, int ST_, int QB_, int NS_, int CPS_>
 struct Cfg {
-  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_;
+  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_, NS = NS_, CPS = CPS_;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
   static constexpr int kKVPanelBytes = BN * 128;
@@ -243,14 +248,18 @@ struct Cfg {
   static constexpr int kOffK = kOffQ + QB * kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
   static constexpr int kOffBar = kOffV + ST * kKVBytes;
-  // barriers: k_full[ST] v_full[ST] kv_empty[ST] q_full[QB] q_empty[QB] s_full[2] p_full[2] pv_done
-  static constexpr int kNumBars = 3 * ST + 2 * QB + 2 + 2 + 1;
+  // barriers: k_full[ST] v_full[ST] kv_empty[ST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS] pv_done o_full
+  static constexpr int kNumBars = 3 * ST + 2 * QB + 2 * NS + 2;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
-  static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColS0 = 0, kColS1 = BN, kColO = 256;
-  static_assert(2 * BN <= 256 && D <= 256, "TMEM budget");
-  static_assert(BN % 32 == 0 && D % 64 == 0, "tile shape");
+  static constexpr uint32_t kColO = NS == 1 ? BN : 256;
+  static constexpr uint32_t kTmemCols = (kColO + D <= 256) ? 256 : 512;
+  // Hold a whole S row in registers only when the register budget allows it.
+  static constexpr bool kOnePass = BN <= 64;
+  static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
+  static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
+  static_assert(BN % 64 == 0 && D % 64 == 0, "tile shape");
+  __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
 };
 
 struct UnitInfo {
@@ -288,8 +297,15 @@ __device__ __forceinline__ UnitInfo unit_info(const AttnParams& p, long long u) 
   return ui;
 }
 
+// Load `n` consecutive 32-column chunks of this warp's TMEM lanes (no wait).
+template <int N>
+__device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[N * 32]) {
+#pragma unroll
+  for (int c = 0; c < N; ++c) tmem_ld32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+}
+
 template <class C>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, C::CPS)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -301,8 +317,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* q_full = kv_empty + C::ST;
   uint64_t* q_empty = q_full + C::QB;
   uint64_t* s_full = q_empty + C::QB;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
+  uint64_t* p_full = s_full + C::NS;
+  uint64_t* pv_done = p_full + C::NS;  // every P.V (O rescale waits on the previous one)
+  uint64_t* o_full = pv_done + 1;       // the last P.V of each unit (epilogue)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -318,11 +335,12 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::NS; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 4);  // one arrival per softmax warp
     }
     mbar_init(pv_done, 1);
+    mbar_init(o_full, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -386,22 +404,24 @@ __global__ void __launch_bounds__(192, 1)
       long long i = 0;
       int lu = 0;
       long long prev_i = -1;
-      int prev_first = 0;
-      auto issue_pv = [&](long long j, int first) {
-        const int sb = (int)(j & 1);
+      int prev_first = 0, prev_last = 0;
+      auto issue_pv = [&](long long j, int first, int last) {
+        const int sb = (int)(j % C::NS);
         const int st = (int)(j % C::ST);
-        mbar_wait(&p_full[sb], (int)(j >> 1) & 1, p.err);
+        mbar_wait(&p_full[sb], (int)(j / C::NS) & 1, p.err);
         mbar_wait(&v_full[st], (int)(j / C::ST) & 1, p.err);
         tc_fence_after();
-        const uint32_t s_col = sb ? C::kColS1 : C::kColS0;
         const uint32_t v_addr = smem_base + C::kOffV + st * C::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk) {
           const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
-          mma_ts(tmem + C::kColO, tmem + s_col + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
+          mma_ts(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
         }
         mma_commit(pv_done);
         mma_commit(&kv_empty[st]);
+        // One completion per unit: with two S buffers the next unit's QK is issued before this
+        // P.V, so S-ready no longer implies earlier P.V completions; the epilogue needs its own.
+        if (last) mma_commit(o_full);
       };
       for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
         const UnitInfo ui = unit_info<C::BN>(p, u);
@@ -412,27 +432,32 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t q_addr = smem_base + C::kOffQ + qb * C::kQBytes;
         for (int t = 0; t < ui.n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
-          const int sb = (int)(i & 1);
+          const int sb = (int)(i % C::NS);
+          // With one S buffer the previous P must be consumed first (issue order = execution order).
+          if (C::NS == 1 && prev_i >= 0) {
+            issue_pv(prev_i, prev_first, prev_last);
+            prev_i = -1;
+          }
           mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
-          const uint32_t s_col = sb ? C::kColS1 : C::kColS0;
 #pragma unroll
           for (int kk = 0; kk < C::D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 0 + (kk & 3) * 32;
+            const uint32_t off = (kk & 3) * 32;
             const uint64_t adesc = sw128_desc(q_addr + (kk >> 2) * C::kQPanelBytes + off, 16, 1024);
             const uint64_t bdesc = sw128_desc(k_addr + (kk >> 2) * C::kKVPanelBytes + off, 16, 1024);
-            mma_ss(tmem + s_col, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+            mma_ss(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[sb]);
           if (t == ui.n_kv - 1) mma_commit(&q_empty[qb]);
-          if (prev_i >= 0) issue_pv(prev_i, prev_first);
+          if (prev_i >= 0) issue_pv(prev_i, prev_first, prev_last);
           prev_i = i;
           prev_first = (t == 0);
+          prev_last = (t == ui.n_kv - 1);
         }
         ++lu;
       }
-      if (prev_i >= 0) issue_pv(prev_i, prev_first);
+      if (prev_i >= 0) issue_pv(prev_i, prev_first, prev_last);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -440,24 +465,30 @@ __global__ void __launch_bounds__(192, 1)
     const int r = quarter * 32 + lane;  // query row of this thread == TMEM lane
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float NEG_INF = -__int_as_float(0x7f800000);
+    const float c2 = p.scale_log2;
     long long i = 0;
+    int lu = 0;
     for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
       const UnitInfo ui = unit_info<C::BN>(p, u);
       if (ui.n_kv == 0) continue;
       // Allowed keys [klo, khi) of this row, in absolute key tokens.
       const bool row_valid = r < ui.nq;
       const int tq = ui.q_row0 + r;
+      int s = ui.f;
+      if (ui.c > 1) {
+        // Packed short sequences: my sequence is f + #(boundaries cu_q[f+1 .. f+c-1] <= tq),
+        // counted with one coalesced load per 32 boundaries and warp shuffles.
+        int cnt = 0;
+        for (int base = 1; base < ui.c; base += 32) {
+          const int idx = base + lane;
+          const int v = idx < ui.c ? p.cu_q[ui.f + idx] : 0x7fffffff;
+#pragma unroll 8
+          for (int j = 0; j < 32; ++j) cnt += (__shfl_sync(0xffffffffu, v, j) <= tq) ? 1 : 0;
+        }
+        s = min(ui.f + cnt, ui.f + ui.c - 1);
+      }
       int klo = 0, khi = 0;
       if (row_valid) {
-        int s = ui.f;
-        if (ui.c > 1) {  // largest s in [f, f + c) with cu_q[s] <= tq
-          int a = ui.f, b = ui.f + ui.c - 1;
-          while (a < b) {
-            int mid = (a + b + 1) >> 1;
-            if (p.cu_q[mid] <= tq) a = mid; else b = mid - 1;
-          }
-          s = a;
-        }
         const int cq = p.cu_q[s], lq = p.cu_q[s + 1] - cq;
         const int ck = p.cu_k[s], lk = p.cu_k[s + 1] - ck;
         const int pos = tq - cq + (lk - lq);
@@ -466,86 +497,146 @@ __global__ void __launch_bounds__(192, 1)
       }
       float m_run = NEG_INF, l_run = 0.f;
       for (int t = 0; t < ui.n_kv; ++t, ++i) {
-        const int sb = (int)(i & 1);
-        const uint32_t s_col = sb ? C::kColS1 : C::kColS0;
+        const int sb = (int)(i % C::NS);
+        const uint32_t s_addr = tmem + lane_base + C::col_s(sb);
         const int kt = ui.kv_lo + t * C::BN;
-        mbar_wait(&s_full[sb], (int)(i >> 1) & 1, p.err);
+        const int c_lo = klo - kt, c_hi = khi - kt;  // valid columns [c_lo, c_hi) of my row
+        // Warp-uniform tile class: every lane's row sees all BN keys (interior tile), and
+        // which 32-key chunks hold any allowed key of any lane of this warp.
+        const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= C::BN);
+        uint32_t active = 0;
+#pragma unroll
+        for (int cc = 0; cc < C::BN / 32; ++cc)
+          active |= (__any_sync(0xffffffffu, c_lo < 32 * (cc + 1) && c_hi > 32 * cc && c_lo < c_hi) ? 1u : 0u) << cc;
+        mbar_wait(&s_full[sb], (int)(i / C::NS) & 1, p.err);
         tc_fence_after();
-        float x[C::BN];
-#pragma unroll
-        for (int cc = 0; cc < C::BN / 32; ++cc) {
-          uint32_t raw[32];
-          tmem_ld32(tmem + lane_base + s_col + cc * 32, raw);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) x[cc * 32 + j] = __uint_as_float(raw[j]);
-        }
+
+        // ---- pass 1: row max of the raw scores (scale > 0 commutes with max)
+        constexpr int kHalf = C::kOnePass ? C::BN : 64;
+        uint32_t raw[kHalf];
         float mx = NEG_INF;
-        const int c_lo = klo - kt, c_hi = khi - kt;  // valid columns [c_lo, c_hi)
 #pragma unroll
-        for (int j = 0; j < C::BN; ++j) {
-          const bool ok = j >= c_lo && j < c_hi;
-          x[j] = ok ? x[j] * p.scale_log2 : NEG_INF;
-          mx = fmaxf(mx, x[j]);
+        for (int h = 0; h < C::BN / kHalf; ++h) {
+#pragma unroll
+          for (int cc = 0; cc < kHalf / 32; ++cc)
+            if (active & (1u << (h * (kHalf / 32) + cc)))
+              tmem_ld32(s_addr + h * kHalf + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+          tmem_wait_ld();
+          if (full) {
+#pragma unroll
+            for (int j = 0; j + 1 < kHalf; j += 2) mx = fmax3(mx, __uint_as_float(raw[j]), __uint_as_float(raw[j + 1]));
+          } else {
+#pragma unroll
+            for (int cc = 0; cc < kHalf / 32; ++cc) {
+              if (!(active & (1u << (h * (kHalf / 32) + cc)))) continue;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int col = h * kHalf + cc * 32 + j;
+                const bool ok = (unsigned)(col - c_lo) < (unsigned)(c_hi - c_lo);
+                raw[cc * 32 + j] = ok ? raw[cc * 32 + j] : __float_as_uint(NEG_INF);
+                mx = fmaxf(mx, __uint_as_float(raw[cc * 32 + j]));
+              }
+            }
+          }
         }
-        const float m_new = fmaxf(m_run, mx);
+        const float m_new = fmaxf(m_run, mx * c2);
         const bool need = (m_run != NEG_INF) && (m_new > m_run + kRescaleThreshold);
-        if (__any_sync(0xffffffffu, need)) {
+        const bool any_need = __any_sync(0xffffffffu, need);
+        const float alpha = need ? ex2(m_run - m_new) : 1.f;
+        if (m_run == NEG_INF || need) m_run = m_new;
+        const float base = (m_run == NEG_INF) ? 0.f : m_run;
+        const float2 cc2 = make_float2(c2, c2), nb2 = make_float2(-base, -base);
+
+        // ---- pass 2: p = exp2(s * scale_log2 - m), bf16 pairs written over S, fp32 row sum
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int h = 0; h < C::BN / kHalf; ++h) {
+          if (!C::kOnePass) {
+#pragma unroll
+            for (int cc = 0; cc < kHalf / 32; ++cc)
+              if (active & (1u << (h * (kHalf / 32) + cc)))
+                tmem_ld32(s_addr + h * kHalf + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+            tmem_wait_ld();
+            if (!full) {
+#pragma unroll
+              for (int cc = 0; cc < kHalf / 32; ++cc) {
+                if (!(active & (1u << (h * (kHalf / 32) + cc)))) continue;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const int col = h * kHalf + cc * 32 + j;
+                  const bool ok = (unsigned)(col - c_lo) < (unsigned)(c_hi - c_lo);
+                  raw[cc * 32 + j] = ok ? raw[cc * 32 + j] : __float_as_uint(NEG_INF);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int cc = 0; cc < kHalf / 32; ++cc) {
+            uint32_t pk[16];
+            if (active & (1u << (h * (kHalf / 32) + cc))) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                float2 x = ffma2(make_float2(__uint_as_float(raw[cc * 32 + 2 * j]), __uint_as_float(raw[cc * 32 + 2 * j + 1])),
+                                 cc2, nb2);
+                float2 e = make_float2(ex2(x.x), ex2(x.y));
+                acc = fadd2(acc, e);
+                pk[j] = pack_bf16x2(e.x, e.y);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) pk[j] = 0u;
+            }
+            tmem_st16(s_addr + (h * kHalf + cc * 32) / 2, pk);
+          }
+        }
+        // O rescale (rare: the running max grew by more than 2^8) after P is out, so the S
+        // registers are free and the previous P.V has had the softmax time to finish.
+        if (any_need) {
           // O holds the sum up to the previous key tile: wait for that P.V to land.
           mbar_wait(pv_done, (int)((i - 1) & 1), p.err);
           tc_fence_after();
-          const float alpha = need ? ex2(m_run - m_new) : 1.f;
 #pragma unroll
-          for (int cc = 0; cc < C::D / 32; ++cc) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_base + C::kColO + cc * 32, o);
+          for (int cc = 0; cc < C::D / 32; cc += 2) {
+            uint32_t o[64];
+            tmem_ld_chunks<2>(tmem + lane_base + C::kColO + cc * 32, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-            tmem_st32(tmem + lane_base + C::kColO + cc * 32, o);
+            for (int j = 0; j < 64; j += 2) {
+              float2 v = fmul2(make_float2(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), make_float2(alpha, alpha));
+              o[j] = __float_as_uint(v.x);
+              o[j + 1] = __float_as_uint(v.y);
+            }
+            tmem_st32(tmem + lane_base + C::kColO + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+            tmem_st32(tmem + lane_base + C::kColO + cc * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
           }
-          tmem_wait_st();
           l_run *= alpha;
         }
-        if (m_run == NEG_INF || need) m_run = m_new;
-        const float base = (m_run == NEG_INF) ? 0.f : m_run;
-        float sum = 0.f;
-#pragma unroll
-        for (int cc = 0; cc < C::BN / 32; ++cc) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float p0 = ex2(x[cc * 32 + 2 * j] - base);
-            const float p1 = ex2(x[cc * 32 + 2 * j + 1] - base);
-            sum += p0 + p1;
-            pk[j] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16(tmem + lane_base + s_col + cc * 16, pk);
-        }
-        l_run += sum;
+        l_run += acc.x + acc.y;
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[sb]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[sb]);
       }
       // Epilogue: O / l -> bf16 rows, LSE in natural log.
-      mbar_wait(pv_done, (int)((i - 1) & 1), p.err);
+      mbar_wait(o_full, lu & 1, p.err);
+      ++lu;
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
       __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head;
 #pragma unroll
-      for (int cc = 0; cc < C::D / 32; ++cc) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_base + C::kColO + cc * 32, o);
+      for (int cc = 0; cc < C::D / 32; cc += 2) {
+        uint32_t o[64];
+        tmem_ld_chunks<2>(tmem + lane_base + C::kColO + cc * 32, o);
         tmem_wait_ld();
-        uint32_t pk[16];
+        uint32_t pk[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < 32; ++j)
           pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
         if (store) {
           uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          for (int j = 0; j < 8; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
         }
       }
       if (store && p.lse != nullptr) {
@@ -746,6 +837,15 @@ static DeviceInfo& device_info(int dev) {
 
 static int block_n_for(int head_dim) { return head_dim == 256 ? 64 : 128; }
 
+// Host-side choice between the two head_dim-64 kernel layouts (read once).
+static int d64_layout() {
+  static int layout = [] {
+    const char* e = getenv("PE_B200_D64_LAYOUT");
+    return (e && strcmp(e, "2x1") == 0) ? 21 : 12;
+  }();
+  return layout;
+}
+
 static long long item_capacity(const PeB200AttnParams* p) {
   return (long long)p->n_seq + (long long)p->total_q / kTileM + 2;
 }
@@ -813,7 +913,8 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   ap.items = reinterpret_cast<const WorkItem*>(static_cast<const uint8_t*>(p->workspace) + kHeaderBytes);
   ap.err = &static_cast<WsHeader*>(p->workspace)->error;
   const long long units = item_capacity(p) * p->heads;
-  const int grid = (int)(units < sms ? units : sms);
+  const long long slots = (long long)sms * C::CPS;
+  const int grid = (int)(units < slots ? units : slots);
   attn_fwd_kernel<C><<<grid, 192, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
   return cudaGetLastError() == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
 }
@@ -890,9 +991,13 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   if (info.supported != 1) return PE_B200_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (p->head_dim) {
-    case 64: return launch_attention<Cfg<64, 128, 3, 2>>(p, s, info.sms);
-    case 128: return launch_attention<Cfg<128, 128, 2, 2>>(p, s, info.sms);
-    case 256: return launch_attention<Cfg<256, 64, 2, 1>>(p, s, info.sms);
+    case 64:
+      // Two layouts of the same kernel: one CTA per SM with a double-buffered S, or two CTAs per
+      // SM with one S each (PE_B200_D64_LAYOUT=2x1 / 1x2; default 1x2).
+      if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 2, 2, 1>>(p, s, info.sms);
+      return launch_attention<Cfg<64, 128, 2, 2, 1, 2>>(p, s, info.sms);
+    case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 1>>(p, s, info.sms);
+    case 256: return launch_attention<Cfg<256, 64, 2, 1, 2, 1>>(p, s, info.sms);
     default: return PE_B200_ERR_UNSUPPORTED;
   }
 }
