@@ -236,9 +236,11 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //   NS  S buffers in TMEM (2: QK of the next key tile overlaps the softmax of this one;
 //       1: a single S, so two CTAs share an SM and overlap each other instead);
 //   CPS CTAs per SM the configuration is sized for (TMEM columns, shared memory, registers).
-template <int D_, int BN_, int ST_, int QB_, int NS_, int CPS_>
+//   POLY of every 16 exp2 pairs evaluated by a cubic on the FMA pipe instead of MUFU (MUFU is the
+//        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
+template <int D_, int BN_, int ST_, int QB_, int NS_, int CPS_, int POLY_>
 struct Cfg {
-  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_, NS = NS_, CPS = CPS_;
+  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
   static constexpr int kKVPanelBytes = BN * 128;
@@ -252,7 +254,7 @@ struct Cfg {
   static constexpr int kNumBars = 3 * ST + 2 * QB + 2 * NS + 2;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
-  static constexpr uint32_t kColO = NS == 1 ? BN : 256;
+  static constexpr uint32_t kColO = NS * BN;
   static constexpr uint32_t kTmemCols = (kColO + D <= 256) ? 256 : 512;
   // Hold a whole S row in registers only when the register budget allows it.
   static constexpr bool kOnePass = BN <= 64;
@@ -296,6 +298,27 @@ __device__ __forceinline__ UnitInfo unit_info(const AttnParams& p, long long u) 
   ui.n_kv = (ui.nq > 0 && kv_hi > kv_lo) ? (kv_hi - kv_lo + BN - 1) / BN : 0;
   return ui;
 }
+
+// The CTA's units (b, b + grid, ...) with the NEXT unit's schedule entry and segment bounds
+// loaded one unit ahead, so their global-load latency hides behind the current unit's work.
+template <int BN>
+struct UnitStream {
+  long long u, n, step;
+  UnitInfo cur, nxt;
+  __device__ __forceinline__ UnitStream(const AttnParams& p, long long first, long long n_units, long long stride)
+      : u(first), n(n_units), step(stride) {
+    cur.n_kv = 0;
+    nxt.n_kv = 0;
+    if (u < n) cur = unit_info<BN>(p, u);
+    if (u + step < n) nxt = unit_info<BN>(p, u + step);
+  }
+  __device__ __forceinline__ bool valid() const { return u < n; }
+  __device__ __forceinline__ void advance(const AttnParams& p) {
+    u += step;
+    cur = nxt;
+    if (u + step < n) nxt = unit_info<BN>(p, u + step);
+  }
+};
 
 // Load `n` consecutive 32-column chunks of this warp's TMEM lanes (no wait).
 template <int N>
@@ -363,8 +386,8 @@ __global__ void __launch_bounds__(192, C::CPS)
     if (lane == 0) {
       long long i = 0;
       int lu = 0;
-      for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const UnitInfo ui = unit_info<C::BN>(p, u);
+      for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
+        const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
         if (lu >= C::QB) mbar_wait(&q_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
@@ -423,8 +446,8 @@ __global__ void __launch_bounds__(192, C::CPS)
         // P.V, so S-ready no longer implies earlier P.V completions; the epilogue needs its own.
         if (last) mma_commit(o_full);
       };
-      for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const UnitInfo ui = unit_info<C::BN>(p, u);
+      for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
+        const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
         mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
@@ -468,8 +491,8 @@ __global__ void __launch_bounds__(192, C::CPS)
     const float c2 = p.scale_log2;
     long long i = 0;
     int lu = 0;
-    for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const UnitInfo ui = unit_info<C::BN>(p, u);
+    for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
+      const UnitInfo ui = us.cur;
       if (ui.n_kv == 0) continue;
       // Allowed keys [klo, khi) of this row, in absolute key tokens.
       const bool row_valid = r < ui.nq;
@@ -514,7 +537,9 @@ __global__ void __launch_bounds__(192, C::CPS)
         // ---- pass 1: row max of the raw scores (scale > 0 commutes with max)
         constexpr int kHalf = C::kOnePass ? C::BN : 64;
         uint32_t raw[kHalf];
-        float mx = NEG_INF;
+        // Four independent max / sum chains: one serial chain per tile would leave the warp
+        // waiting on its own latency.
+        float mxs[4] = {NEG_INF, NEG_INF, NEG_INF, NEG_INF};
 #pragma unroll
         for (int h = 0; h < C::BN / kHalf; ++h) {
 #pragma unroll
@@ -524,7 +549,8 @@ __global__ void __launch_bounds__(192, C::CPS)
           tmem_wait_ld();
           if (full) {
 #pragma unroll
-            for (int j = 0; j + 1 < kHalf; j += 2) mx = fmax3(mx, __uint_as_float(raw[j]), __uint_as_float(raw[j + 1]));
+            for (int j = 0; j + 1 < kHalf; j += 2)
+              mxs[(j >> 1) & 3] = fmax3(mxs[(j >> 1) & 3], __uint_as_float(raw[j]), __uint_as_float(raw[j + 1]));
           } else {
 #pragma unroll
             for (int cc = 0; cc < kHalf / 32; ++cc) {
@@ -534,11 +560,12 @@ __global__ void __launch_bounds__(192, C::CPS)
                 const int col = h * kHalf + cc * 32 + j;
                 const bool ok = (unsigned)(col - c_lo) < (unsigned)(c_hi - c_lo);
                 raw[cc * 32 + j] = ok ? raw[cc * 32 + j] : __float_as_uint(NEG_INF);
-                mx = fmaxf(mx, __uint_as_float(raw[cc * 32 + j]));
+                mxs[j & 3] = fmaxf(mxs[j & 3], __uint_as_float(raw[cc * 32 + j]));
               }
             }
           }
         }
+        const float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
         const float m_new = fmaxf(m_run, mx * c2);
         const bool need = (m_run != NEG_INF) && (m_new > m_run + kRescaleThreshold);
         const bool any_need = __any_sync(0xffffffffu, need);
@@ -548,7 +575,7 @@ __global__ void __launch_bounds__(192, C::CPS)
         const float2 cc2 = make_float2(c2, c2), nb2 = make_float2(-base, -base);
 
         // ---- pass 2: p = exp2(s * scale_log2 - m), bf16 pairs written over S, fp32 row sum
-        float2 acc = make_float2(0.f, 0.f);
+        float2 accs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int h = 0; h < C::BN / kHalf; ++h) {
           if (!C::kOnePass) {
@@ -578,8 +605,8 @@ __global__ void __launch_bounds__(192, C::CPS)
               for (int j = 0; j < 16; ++j) {
                 float2 x = ffma2(make_float2(__uint_as_float(raw[cc * 32 + 2 * j]), __uint_as_float(raw[cc * 32 + 2 * j + 1])),
                                  cc2, nb2);
-                float2 e = make_float2(ex2(x.x), ex2(x.y));
-                acc = fadd2(acc, e);
+                float2 e = (j < C::POLY) ? ex2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+                accs[j & 3] = fadd2(accs[j & 3], e);
                 pk[j] = pack_bf16x2(e.x, e.y);
               }
             } else {
@@ -596,21 +623,21 @@ __global__ void __launch_bounds__(192, C::CPS)
           mbar_wait(pv_done, (int)((i - 1) & 1), p.err);
           tc_fence_after();
 #pragma unroll
-          for (int cc = 0; cc < C::D / 32; cc += 2) {
-            uint32_t o[64];
-            tmem_ld_chunks<2>(tmem + lane_base + C::kColO + cc * 32, o);
+          for (int cc = 0; cc < C::D / 32; ++cc) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_base + C::kColO + cc * 32, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 64; j += 2) {
+            for (int j = 0; j < 32; j += 2) {
               float2 v = fmul2(make_float2(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), make_float2(alpha, alpha));
               o[j] = __float_as_uint(v.x);
               o[j + 1] = __float_as_uint(v.y);
             }
-            tmem_st32(tmem + lane_base + C::kColO + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-            tmem_st32(tmem + lane_base + C::kColO + cc * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+            tmem_st32(tmem + lane_base + C::kColO + cc * 32, o);
           }
           l_run *= alpha;
         }
+        const float2 acc = fadd2(fadd2(accs[0], accs[1]), fadd2(accs[2], accs[3]));
         l_run += acc.x + acc.y;
         tmem_wait_st();
         tc_fence_before();
@@ -624,19 +651,20 @@ __global__ void __launch_bounds__(192, C::CPS)
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
       __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head;
+      constexpr int kEpi = C::CPS == 1 ? 2 : 1;  // 32-column chunks per TMEM load (register budget)
 #pragma unroll
-      for (int cc = 0; cc < C::D / 32; cc += 2) {
-        uint32_t o[64];
-        tmem_ld_chunks<2>(tmem + lane_base + C::kColO + cc * 32, o);
+      for (int cc = 0; cc < C::D / 32; cc += kEpi) {
+        uint32_t o[kEpi * 32];
+        tmem_ld_chunks<kEpi>(tmem + lane_base + C::kColO + cc * 32, o);
         tmem_wait_ld();
-        uint32_t pk[32];
+        uint32_t pk[kEpi * 16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
+        for (int j = 0; j < kEpi * 16; ++j)
           pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
         if (store) {
           uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          for (int j = 0; j < kEpi * 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
         }
       }
       if (store && p.lse != nullptr) {
@@ -837,11 +865,19 @@ static DeviceInfo& device_info(int dev) {
 
 static int block_n_for(int head_dim) { return head_dim == 256 ? 64 : 128; }
 
+// Integer from the environment (tuning knobs), read on every call.
+static int env_int(const char* name, int fallback) {
+  const char* e = getenv(name);
+  return (e && *e) ? atoi(e) : fallback;
+}
+
 // Host-side choice between the two head_dim-64 kernel layouts (read once).
 static int d64_layout() {
   static int layout = [] {
     const char* e = getenv("PE_B200_D64_LAYOUT");
-    return (e && strcmp(e, "2x1") == 0) ? 21 : 12;
+    if (e && strcmp(e, "2x1") == 0) return 21;   // BN=128, two S buffers, one CTA per SM
+    if (e && strcmp(e, "1x2") == 0) return 12;   // BN=128, one S buffer, two CTAs per SM
+    return 22;                                    // BN=64, two S buffers, two CTAs per SM
   }();
   return layout;
 }
@@ -992,12 +1028,17 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (p->head_dim) {
     case 64:
-      // Two layouts of the same kernel: one CTA per SM with a double-buffered S, or two CTAs per
-      // SM with one S each (PE_B200_D64_LAYOUT=2x1 / 1x2; default 1x2).
-      if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 2, 2, 1>>(p, s, info.sms);
-      return launch_attention<Cfg<64, 128, 2, 2, 1, 2>>(p, s, info.sms);
-    case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 1>>(p, s, info.sms);
-    case 256: return launch_attention<Cfg<256, 64, 2, 1, 2, 1>>(p, s, info.sms);
+      // Layouts of the same kernel (PE_B200_D64_LAYOUT): default 64-key tiles, two S buffers and
+      // two CTAs per SM; 2x1 / 1x2 are the 128-key-tile variants kept for comparison.
+      if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 2, 2, 1, 8>>(p, s, info.sms);
+      if (d64_layout() == 12) return launch_attention<Cfg<64, 128, 2, 2, 1, 2, 0>>(p, s, info.sms);
+      switch (env_int("PE_B200_D64_POLY", 0)) {  // tuning knob: exp2 pairs (of 16) on the FMA pipe
+        case 4: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 4>>(p, s, info.sms);
+        case 8: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 8>>(p, s, info.sms);
+        default: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 0>>(p, s, info.sms);
+      }
+    case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 1, 4>>(p, s, info.sms);
+    case 256: return launch_attention<Cfg<256, 64, 2, 1, 2, 1, 0>>(p, s, info.sms);
     default: return PE_B200_ERR_UNSUPPORTED;
   }
 }

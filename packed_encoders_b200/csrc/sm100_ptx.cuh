@@ -248,6 +248,28 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
   return d;
 }
 
+// 2^x for a pair of x <= 0 on the FMA pipe (no MUFU): round x to the nearest integer j with the
+// 1.5 * 2^23 magic-number add, evaluate 2^(x - j) on [-0.5, 0.5] with a cubic, add j to the
+// exponent. The cubic is a relative least-squares fit made for this kernel (max relative error
+// 7.5e-5 in fp32, far below the 2^-9 of the bf16 P it feeds). x is clamped at -125 so the
+// biased exponent of the result stays >= 1 (2^(x-j) >= 2^-0.5 has biased exponent >= 126);
+// 2^-125 stands in for exp2(-inf) (it is 0 in every sum it enters to fp32 precision).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 magic = make_float2(12582912.f, 12582912.f);
+  const float2 t = fadd2(x, magic);
+  const float2 j = fadd2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = ffma2(j, make_float2(-1.f, -1.f), x);
+  float2 p = ffma2(make_float2(0.05517115443944931f, 0.05517115443944931f), f,
+                   make_float2(0.2426101416349411f, 0.2426101416349411f));
+  p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, make_float2(0.9999281167984009f, 0.9999281167984009f));
+  const uint32_t bx = __float_as_uint(p.x) + (__float_as_uint(t.x) << 23);
+  const uint32_t by = __float_as_uint(p.y) + (__float_as_uint(t.y) << 23);
+  return make_float2(__uint_as_float(bx), __uint_as_float(by));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
