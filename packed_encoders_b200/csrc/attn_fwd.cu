@@ -238,9 +238,12 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //   CPS CTAs per SM the configuration is sized for (TMEM columns, shared memory, registers).
 //   POLY of every 16 exp2 pairs evaluated by a cubic on the FMA pipe instead of MUFU (MUFU is the
 //        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
-template <int D_, int BN_, int ST_, int QB_, int NS_, int CPS_, int POLY_>
+//   SPLIT softmax warps per 32-row TMEM lane quarter, each owning 1/SPLIT of the key columns and
+//        of O (more warps to hide latency at the same registers per row).
+template <int D_, int BN_, int ST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1>
 struct Cfg {
-  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_;
+  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_, SPLIT = SPLIT_;
+  static constexpr int kThreads = 64 + 128 * SPLIT;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
   static constexpr int kKVPanelBytes = BN * 128;
@@ -253,14 +256,15 @@ struct Cfg {
   // barriers: k_full[ST] v_full[ST] kv_empty[ST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS] pv_done o_full
   static constexpr int kNumBars = 3 * ST + 2 * QB + 2 * NS + 2;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
-  static constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;  // + alignment slack
+  static constexpr int kOffXchg = kOffTmemSlot + 16;  // row max [2][SPLIT][128] and sum [SPLIT][128], fp32
+  static constexpr int kSmemBytes = kOffXchg + (SPLIT > 1 ? 3 * SPLIT * kTileM * 4 : 0) + 1024;  // + align slack
   static constexpr uint32_t kColO = NS * BN;
-  static constexpr uint32_t kTmemCols = (kColO + D <= 256) ? 256 : 512;
+  static constexpr uint32_t kTmemCols = (kColO + D <= 128) ? 128 : (kColO + D <= 256) ? 256 : 512;
   // Hold a whole S row in registers only when the register budget allows it.
-  static constexpr bool kOnePass = BN <= 64;
   static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
   static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
   static_assert(BN % 64 == 0 && D % 64 == 0, "tile shape");
+  static_assert((BN / SPLIT) % 32 == 0 && (D / SPLIT) % 32 == 0 && SPLIT <= 2, "column split");
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
 };
 
@@ -328,7 +332,7 @@ __device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[N *
 }
 
 template <class C>
-__global__ void __launch_bounds__(192, C::CPS)
+__global__ void __launch_bounds__(C::kThreads, C::CPS)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -360,7 +364,7 @@ __global__ void __launch_bounds__(192, C::CPS)
     }
     for (int i = 0; i < C::NS; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);  // one arrival per softmax warp
+      mbar_init(&p_full[i], 4 * C::SPLIT);  // one arrival per softmax warp
     }
     mbar_init(pv_done, 1);
     mbar_init(o_full, 1);
@@ -484,11 +488,26 @@ __global__ void __launch_bounds__(192, C::CPS)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
+    // SPLIT warps share each 32-row TMEM lane quarter: warp (2 + 4*h + q') owns key columns
+    // [h*BN/SPLIT, (h+1)*BN/SPLIT) of every S tile and O columns [h*D/SPLIT, ...) of rows
+    // 32*q'.. (q' = warp % 4); row maxima and sums are exchanged through shared memory.
+    constexpr int kCols = C::BN / C::SPLIT;     // S columns per thread per key tile
+    constexpr int kPass = kCols < 64 ? kCols : 64;  // S columns held in registers at once
+    constexpr int kOCols = C::D / C::SPLIT;     // O columns per thread
+    const int sw = warp - 2;
+    const int half = sw >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row of this thread == TMEM lane
+    const int col0 = half * kCols;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t o_addr = tmem + lane_base + C::kColO + half * kOCols;
     const float NEG_INF = -__int_as_float(0x7f800000);
     const float c2 = p.scale_log2;
+    float* xmax = reinterpret_cast<float*>(smem + C::kOffXchg);     // [2 parity][SPLIT][128]
+    float* xsum = xmax + 2 * C::SPLIT * kTileM;                      // [SPLIT][128]
+    auto pair_sync = [&]() {  // the SPLIT warps of this lane quarter
+      if (C::SPLIT > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(32 * C::SPLIT) : "memory");
+    };
     long long i = 0;
     int lu = 0;
     for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
@@ -523,41 +542,40 @@ __global__ void __launch_bounds__(192, C::CPS)
         const int sb = (int)(i % C::NS);
         const uint32_t s_addr = tmem + lane_base + C::col_s(sb);
         const int kt = ui.kv_lo + t * C::BN;
-        const int c_lo = klo - kt, c_hi = khi - kt;  // valid columns [c_lo, c_hi) of my row
-        // Warp-uniform tile class: every lane's row sees all BN keys (interior tile), and
-        // which 32-key chunks hold any allowed key of any lane of this warp.
-        const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= C::BN);
+        // Valid columns of my row, relative to my first column: [c_lo, c_hi).
+        const int c_lo = klo - kt - col0, c_hi = khi - kt - col0;
+        // Warp-uniform: every lane's row sees all my columns (interior tile), and which of my
+        // 32-column chunks hold any allowed key of any lane of this warp.
+        const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= kCols);
         uint32_t active = 0;
 #pragma unroll
-        for (int cc = 0; cc < C::BN / 32; ++cc)
+        for (int cc = 0; cc < kCols / 32; ++cc)
           active |= (__any_sync(0xffffffffu, c_lo < 32 * (cc + 1) && c_hi > 32 * cc && c_lo < c_hi) ? 1u : 0u) << cc;
         mbar_wait(&s_full[sb], (int)(i / C::NS) & 1, p.err);
         tc_fence_after();
 
-        // ---- pass 1: row max of the raw scores (scale > 0 commutes with max)
-        constexpr int kHalf = C::kOnePass ? C::BN : 64;
-        uint32_t raw[kHalf];
-        // Four independent max / sum chains: one serial chain per tile would leave the warp
-        // waiting on its own latency.
+        // ---- pass 1: row max of the raw scores (scale > 0 commutes with max); four
+        // independent chains so the warp does not wait on its own latency.
+        uint32_t raw[kPass];
         float mxs[4] = {NEG_INF, NEG_INF, NEG_INF, NEG_INF};
 #pragma unroll
-        for (int h = 0; h < C::BN / kHalf; ++h) {
+        for (int h = 0; h < kCols / kPass; ++h) {
 #pragma unroll
-          for (int cc = 0; cc < kHalf / 32; ++cc)
-            if (active & (1u << (h * (kHalf / 32) + cc)))
-              tmem_ld32(s_addr + h * kHalf + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+          for (int cc = 0; cc < kPass / 32; ++cc)
+            if (active & (1u << (h * (kPass / 32) + cc)))
+              tmem_ld32(s_addr + col0 + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
           tmem_wait_ld();
           if (full) {
 #pragma unroll
-            for (int j = 0; j + 1 < kHalf; j += 2)
+            for (int j = 0; j + 1 < kPass; j += 2)
               mxs[(j >> 1) & 3] = fmax3(mxs[(j >> 1) & 3], __uint_as_float(raw[j]), __uint_as_float(raw[j + 1]));
           } else {
 #pragma unroll
-            for (int cc = 0; cc < kHalf / 32; ++cc) {
-              if (!(active & (1u << (h * (kHalf / 32) + cc)))) continue;
+            for (int cc = 0; cc < kPass / 32; ++cc) {
+              if (!(active & (1u << (h * (kPass / 32) + cc)))) continue;
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const int col = h * kHalf + cc * 32 + j;
+                const int col = h * kPass + cc * 32 + j;
                 const bool ok = (unsigned)(col - c_lo) < (unsigned)(c_hi - c_lo);
                 raw[cc * 32 + j] = ok ? raw[cc * 32 + j] : __float_as_uint(NEG_INF);
                 mxs[j & 3] = fmaxf(mxs[j & 3], __uint_as_float(raw[cc * 32 + j]));
@@ -565,7 +583,15 @@ __global__ void __launch_bounds__(192, C::CPS)
             }
           }
         }
-        const float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
+        float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
+        if (C::SPLIT > 1) {  // combine with the other column halves of my row
+          float* slot = xmax + ((int)(i & 1) * C::SPLIT) * kTileM;
+          slot[half * kTileM + r] = mx;
+          pair_sync();
+#pragma unroll
+          for (int o = 0; o < C::SPLIT; ++o)
+            if (o != half) mx = fmaxf(mx, slot[o * kTileM + r]);
+        }
         const float m_new = fmaxf(m_run, mx * c2);
         const bool need = (m_run != NEG_INF) && (m_new > m_run + kRescaleThreshold);
         const bool any_need = __any_sync(0xffffffffu, need);
@@ -577,20 +603,20 @@ __global__ void __launch_bounds__(192, C::CPS)
         // ---- pass 2: p = exp2(s * scale_log2 - m), bf16 pairs written over S, fp32 row sum
         float2 accs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int h = 0; h < C::BN / kHalf; ++h) {
-          if (!C::kOnePass) {
+        for (int h = 0; h < kCols / kPass; ++h) {
+          if (kCols > kPass) {  // S did not fit in registers: reload this pass's columns
 #pragma unroll
-            for (int cc = 0; cc < kHalf / 32; ++cc)
-              if (active & (1u << (h * (kHalf / 32) + cc)))
-                tmem_ld32(s_addr + h * kHalf + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+            for (int cc = 0; cc < kPass / 32; ++cc)
+              if (active & (1u << (h * (kPass / 32) + cc)))
+                tmem_ld32(s_addr + col0 + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
             tmem_wait_ld();
             if (!full) {
 #pragma unroll
-              for (int cc = 0; cc < kHalf / 32; ++cc) {
-                if (!(active & (1u << (h * (kHalf / 32) + cc)))) continue;
+              for (int cc = 0; cc < kPass / 32; ++cc) {
+                if (!(active & (1u << (h * (kPass / 32) + cc)))) continue;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                  const int col = h * kHalf + cc * 32 + j;
+                  const int col = h * kPass + cc * 32 + j;
                   const bool ok = (unsigned)(col - c_lo) < (unsigned)(c_hi - c_lo);
                   raw[cc * 32 + j] = ok ? raw[cc * 32 + j] : __float_as_uint(NEG_INF);
                 }
@@ -598,9 +624,9 @@ __global__ void __launch_bounds__(192, C::CPS)
             }
           }
 #pragma unroll
-          for (int cc = 0; cc < kHalf / 32; ++cc) {
+          for (int cc = 0; cc < kPass / 32; ++cc) {
             uint32_t pk[16];
-            if (active & (1u << (h * (kHalf / 32) + cc))) {
+            if (active & (1u << (h * (kPass / 32) + cc))) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 float2 x = ffma2(make_float2(__uint_as_float(raw[cc * 32 + 2 * j]), __uint_as_float(raw[cc * 32 + 2 * j + 1])),
@@ -613,7 +639,7 @@ __global__ void __launch_bounds__(192, C::CPS)
 #pragma unroll
               for (int j = 0; j < 16; ++j) pk[j] = 0u;
             }
-            tmem_st16(s_addr + (h * kHalf + cc * 32) / 2, pk);
+            tmem_st16(s_addr + (col0 + h * kPass + cc * 32) / 2, pk);
           }
         }
         // O rescale (rare: the running max grew by more than 2^8) after P is out, so the S
@@ -623,9 +649,9 @@ __global__ void __launch_bounds__(192, C::CPS)
           mbar_wait(pv_done, (int)((i - 1) & 1), p.err);
           tc_fence_after();
 #pragma unroll
-          for (int cc = 0; cc < C::D / 32; ++cc) {
+          for (int cc = 0; cc < kOCols / 32; ++cc) {
             uint32_t o[32];
-            tmem_ld32(tmem + lane_base + C::kColO + cc * 32, o);
+            tmem_ld32(o_addr + cc * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
@@ -633,7 +659,7 @@ __global__ void __launch_bounds__(192, C::CPS)
               o[j] = __float_as_uint(v.x);
               o[j + 1] = __float_as_uint(v.y);
             }
-            tmem_st32(tmem + lane_base + C::kColO + cc * 32, o);
+            tmem_st32(o_addr + cc * 32, o);
           }
           l_run *= alpha;
         }
@@ -644,18 +670,26 @@ __global__ void __launch_bounds__(192, C::CPS)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[sb]);
       }
-      // Epilogue: O / l -> bf16 rows, LSE in natural log.
+      // Epilogue: O / l -> bf16 rows (my O columns), LSE in natural log.
+      if (C::SPLIT > 1) {  // l is split over the column halves
+        xsum[half * kTileM + r] = l_run;
+        pair_sync();
+        float l_all = 0.f;
+#pragma unroll
+        for (int o = 0; o < C::SPLIT; ++o) l_all += (o == half) ? l_run : xsum[o * kTileM + r];
+        l_run = l_all;
+      }
       mbar_wait(o_full, lu & 1, p.err);
       ++lu;
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
-      __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head;
-      constexpr int kEpi = C::CPS == 1 ? 2 : 1;  // 32-column chunks per TMEM load (register budget)
+      __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head + half * kOCols;
+      constexpr int kEpi = (C::CPS == 1 && C::SPLIT == 1) ? 2 : 1;  // 32-column chunks per TMEM load
 #pragma unroll
-      for (int cc = 0; cc < C::D / 32; cc += kEpi) {
+      for (int cc = 0; cc < kOCols / 32; cc += kEpi) {
         uint32_t o[kEpi * 32];
-        tmem_ld_chunks<kEpi>(tmem + lane_base + C::kColO + cc * 32, o);
+        tmem_ld_chunks<kEpi>(o_addr + cc * 32, o);
         tmem_wait_ld();
         uint32_t pk[kEpi * 16];
 #pragma unroll
@@ -667,7 +701,7 @@ __global__ void __launch_bounds__(192, C::CPS)
           for (int j = 0; j < kEpi * 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
         }
       }
-      if (store && p.lse != nullptr) {
+      if (store && half == 0 && p.lse != nullptr) {
         const float lse = l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : NEG_INF;
         p.lse[(long long)ui.head * p.total_q + tq] = lse;
       }
@@ -877,7 +911,8 @@ static int d64_layout() {
     const char* e = getenv("PE_B200_D64_LAYOUT");
     if (e && strcmp(e, "2x1") == 0) return 21;   // BN=128, two S buffers, one CTA per SM
     if (e && strcmp(e, "1x2") == 0) return 12;   // BN=128, one S buffer, two CTAs per SM
-    return 22;                                    // BN=64, two S buffers, two CTAs per SM
+    if (e && strcmp(e, "split") == 0) return 23; // as the default with two softmax warps per row (column halves)
+    return 22;                                    // BN=64, two S buffers, two CTAs per SM, one warp per row
   }();
   return layout;
 }
@@ -951,7 +986,7 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   const long long units = item_capacity(p) * p->heads;
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
-  attn_fwd_kernel<C><<<grid, 192, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
+  attn_fwd_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
   return cudaGetLastError() == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
 }
 
@@ -1032,10 +1067,11 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
       // two CTAs per SM; 2x1 / 1x2 are the 128-key-tile variants kept for comparison.
       if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 2, 2, 1, 8>>(p, s, info.sms);
       if (d64_layout() == 12) return launch_attention<Cfg<64, 128, 2, 2, 1, 2, 0>>(p, s, info.sms);
+      if (d64_layout() == 23) return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 0, 2>>(p, s, info.sms);
       switch (env_int("PE_B200_D64_POLY", 0)) {  // tuning knob: exp2 pairs (of 16) on the FMA pipe
-        case 4: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 4>>(p, s, info.sms);
-        case 8: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 8>>(p, s, info.sms);
-        default: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 0>>(p, s, info.sms);
+        case 4: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 4, 1>>(p, s, info.sms);
+        case 8: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 8, 1>>(p, s, info.sms);
+        default: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 0, 1>>(p, s, info.sms);
       }
     case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 1, 4>>(p, s, info.sms);
     case 256: return launch_attention<Cfg<256, 64, 2, 1, 2, 1, 0>>(p, s, info.sms);
