@@ -1,0 +1,104 @@
+"""Host-side wiring of the "b200" backend into the reference package (no GPU needed).
+
+The reference's own tests do the same with monkeypatched loaders
+(tests/test_attention_backend.py:29-120): the kernels are replaced by a recorder here.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+for candidate in (ROOT / "baseline" / "_ref", Path("/root/reference")):
+    if (candidate / "packed_encoders" / "__init__.py").exists() and str(candidate) not in sys.path:
+        sys.path.append(str(candidate))
+        break
+
+pe_ref = pytest.importorskip("packed_encoders")
+
+
+@pytest.fixture(scope="module")
+def installed():
+    from packed_encoders_b200 import install
+
+    install.install()
+    return install
+
+
+def test_install_is_idempotent_and_patches_hooks(installed):
+    import importlib
+
+    forward = importlib.import_module("packed_encoders.forward")
+    ops = importlib.import_module("packed_encoders.ops")
+    pack = importlib.import_module("packed_encoders.pack")
+    rt = importlib.import_module("packed_encoders.runtime.attention")
+
+    installed.install()
+    assert "b200" in rt._CANDIDATES
+    assert ops.attention_bshd.__wrapped__ is not None
+    assert pack._prepare_modernbert.__wrapped__ is not None
+    assert forward.fused_forward.__wrapped__ is not None
+    with torch.no_grad():
+        assert ops.use_bshd_rope_flash("b200", 12, 64, None)
+    assert not ops.use_bshd_rope_flash("b200", 12, 64, None) if torch.is_grad_enabled() else True
+    # an unknown backend still behaves as before
+    with torch.no_grad():
+        assert not ops.use_bshd_rope_flash("sdpa", 12, 64, None)
+
+
+def test_backend_resolution_keeps_b200(installed):
+    from packed_encoders import attention_dispatch, forward
+
+    workload = attention_dispatch.AttentionWorkload.from_lengths([5, 300, 17])
+    assert forward._resolve_eager_backend("b200", workload, triton_supported=True, flash_available=True) == "b200"
+
+
+def test_candidate_forms_call_the_kernels(installed, monkeypatch):
+    from packed_encoders_b200 import ops as b200_ops
+
+    calls = []
+
+    def recorder(q, k, v, cu, max_len, **kw):
+        calls.append((cu, max_len, kw))
+        return torch.zeros_like(q)
+
+    monkeypatch.setattr(b200_ops, "packed_attention", recorder)
+    packed, padded, prefixed = installed.b200_candidate((16, 16), 0.125)
+    q = torch.zeros(10, 4, 64)
+    k = torch.zeros(10, 2, 64)
+    cu = torch.tensor([0, 4, 10], dtype=torch.int32)
+    packed(q, k, k, cu, 6, [4, 6], True)
+    assert calls[-1][1] == 6 and calls[-1][2]["causal"] and calls[-1][2]["window"] == (16, 16)
+
+    class Static:
+        seg_cu32 = torch.tensor([0, 3, 5, 5, 10], dtype=torch.int32)
+        seq = 5
+
+    padded(q, k, k, Static, False)
+    assert calls[-1][0] is Static.seg_cu32 and calls[-1][1] == 5
+    cu_k = torch.tensor([0, 6, 14], dtype=torch.int32)
+    prefixed(q, torch.zeros(14, 2, 64), torch.zeros(14, 2, 64), cu, cu_k, 6, 8, [4, 6], [6, 8], True)
+    assert calls[-1][2]["cu_seqlens_k"] is cu_k and calls[-1][2]["max_seqlen_k"] == 8
+
+
+def test_b200_piece_contract(installed):
+    from packed_encoders.pieces.attention import BSHD
+
+    piece = installed.b200_attention_bshd_piece()
+    assert piece.contract == BSHD
+    q = torch.zeros(1, 10, 2, 64)
+    with pytest.raises(Exception):  # the rectangular form is not served
+        piece.check(q, q, q, window=(-1, -1), scaling=0.125, backend="flash")
+
+
+def test_attention_leaf_refuses_rectangular_b200(installed):
+    from packed_encoders import ops
+    from packed_encoders_b200.errors import UnsupportedTargetError
+
+    q = torch.zeros(1, 2, 10, 64)
+    with pytest.raises(UnsupportedTargetError):
+        ops.attention(q, q, q, mask=None, window=(-1, -1), scaling=0.125, backend="b200")
