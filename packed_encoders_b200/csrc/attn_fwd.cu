@@ -232,7 +232,8 @@ __global__ void clear_header_kernel(WsHeader* h) {
 
 // ---------------------------------------------------------------------------------------------
 // Attention kernel configuration.
-//   D   head_dim;  BN key-tile rows;  ST K/V ring stages;  QB Q-tile buffers;
+//   D   head_dim;  BN key-tile rows;  ST / VST K / V ring stages (K is released after QK, V after
+//       P.V, and K runs one key tile ahead of V);  QB Q-tile buffers;
 //   NS  S buffers in TMEM (2: QK of the next key tile overlaps the softmax of this one;
 //       1: a single S, so two CTAs share an SM and overlap each other instead);
 //   CPS CTAs per SM the configuration is sized for (TMEM columns, shared memory, registers).
@@ -240,9 +241,10 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
 //   SPLIT softmax warps per 32-row TMEM lane quarter, each owning 1/SPLIT of the key columns and
 //        of O (more warps to hide latency at the same registers per row).
-template <int D_, int BN_, int ST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1>
+template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1>
 struct Cfg {
-  static constexpr int D = D_, BN = BN_, ST = ST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_, SPLIT = SPLIT_;
+  static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_,
+                       SPLIT = SPLIT_;
   static constexpr int kThreads = 64 + 128 * SPLIT;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
@@ -252,12 +254,19 @@ struct Cfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + QB * kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
-  static constexpr int kOffBar = kOffV + ST * kKVBytes;
-  // barriers: k_full[ST] v_full[ST] kv_empty[ST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS] pv_done o_full
-  static constexpr int kNumBars = 3 * ST + 2 * QB + 2 * NS + 2;
+  static constexpr int kOffBar = kOffV + VST * kKVBytes;
+  // barriers: k_full[ST] k_empty[ST] v_full[VST] v_empty[VST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS]
+  //           pv_done o_full
+  static constexpr int kNumBars = 2 * ST + 2 * VST + 2 * QB + 2 * NS + 2;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr int kOffXchg = kOffTmemSlot + 16;  // row max [2][SPLIT][128] and sum [SPLIT][128], fp32
-  static constexpr int kSmemBytes = kOffXchg + (SPLIT > 1 ? 3 * SPLIT * kTileM * 4 : 0) + 1024;  // + align slack
+  static constexpr int kXchgBytes = SPLIT > 1 ? 3 * SPLIT * kTileM * 4 : 0;
+  // Epilogue staging (2 KB per softmax warp) so output rows leave as coalesced 128-byte lines;
+  // only where shared memory allows (head_dim 64).
+  static constexpr bool kStageOut = (D / SPLIT) == 64 && CPS > 1;
+  static constexpr int kOffStage = (kOffXchg + kXchgBytes + 127) & ~127;
+  static constexpr int kStageBytes = kStageOut ? 4 * SPLIT * 2048 : 0;
+  static constexpr int kSmemBytes = kOffStage + kStageBytes + 1024;  // + align slack
   static constexpr uint32_t kColO = NS * BN;
   static constexpr uint32_t kTmemCols = (kColO + D <= 128) ? 128 : (kColO + D <= 256) ? 256 : 512;
   // Hold a whole S row in registers only when the register budget allows it.
@@ -303,6 +312,54 @@ __device__ __forceinline__ UnitInfo unit_info(const AttnParams& p, long long u) 
   return ui;
 }
 
+template <int BN>
+__device__ __forceinline__ UnitInfo unit_info_from(const AttnParams& p, const WorkItem& it, long long u) {
+  UnitInfo ui;
+  ui.head = (int)(u % p.heads);
+  ui.kv_head = ui.head / p.group;
+  ui.f = it.seq_first;
+  ui.c = it.seq_count;
+  ui.qb = it.q_block;
+  const int cq0 = p.cu_q[ui.f], cqe = p.cu_q[ui.f + ui.c];
+  ui.q_row0 = cq0 + ui.qb * kTileM;
+  ui.nq = min(kTileM, cqe - ui.q_row0);
+  int kv_lo, kv_hi;
+  if (ui.c == 1) {
+    const int ck0 = p.cu_k[ui.f];
+    int lo, hi;
+    block_key_range(ui.qb, ui.nq, cqe - cq0, p.cu_k[ui.f + 1] - ck0, p.window_left, p.window_right, lo, hi);
+    kv_lo = ck0 + lo;
+    kv_hi = ck0 + hi;
+  } else {
+    kv_lo = p.cu_k[ui.f];
+    kv_hi = p.cu_k[ui.f + ui.c];
+  }
+  ui.kv_lo = kv_lo;
+  ui.n_kv = (ui.nq > 0 && kv_hi > kv_lo) ? (kv_hi - kv_lo + BN - 1) / BN : 0;
+  return ui;
+}
+
+// Lighter variant for the register-bound softmax warps: only the next work item (16 bytes) is
+// loaded one unit ahead; the segment bounds are read when the unit starts.
+template <int BN>
+struct ItemStream {
+  long long u, n, step;
+  WorkItem nxt;
+  UnitInfo cur;
+  __device__ __forceinline__ ItemStream(const AttnParams& p, long long first, long long n_units, long long stride)
+      : u(first), n(n_units), step(stride) {
+    cur.n_kv = 0;
+    if (u < n) cur = unit_info_from<BN>(p, p.items[u / p.heads], u);
+    if (u + step < n) nxt = p.items[(u + step) / p.heads];
+  }
+  __device__ __forceinline__ bool valid() const { return u < n; }
+  __device__ __forceinline__ void advance(const AttnParams& p) {
+    u += step;
+    if (u < n) cur = unit_info_from<BN>(p, nxt, u);
+    if (u + step < n) nxt = p.items[(u + step) / p.heads];
+  }
+};
+
 // The CTA's units (b, b + grid, ...) with the NEXT unit's schedule entry and segment bounds
 // loaded one unit ahead, so their global-load latency hides behind the current unit's work.
 template <int BN>
@@ -339,9 +396,10 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* k_full = bars;
-  uint64_t* v_full = k_full + C::ST;
-  uint64_t* kv_empty = v_full + C::ST;
-  uint64_t* q_full = kv_empty + C::ST;
+  uint64_t* k_empty = k_full + C::ST;
+  uint64_t* v_full = k_empty + C::ST;
+  uint64_t* v_empty = v_full + C::VST;
+  uint64_t* q_full = v_empty + C::VST;
   uint64_t* q_empty = q_full + C::QB;
   uint64_t* s_full = q_empty + C::QB;
   uint64_t* p_full = s_full + C::NS;
@@ -355,8 +413,11 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::ST; ++i) {
       mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < C::VST; ++i) {
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < C::QB; ++i) {
       mbar_init(&q_full[i], 1);
@@ -388,8 +449,19 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      long long i = 0;
+      long long i = 0;  // key tiles whose K is issued; V of tile i-1 follows K of tile i
       int lu = 0;
+      int v_row = 0, v_head = 0;
+      bool v_pending = false;
+      auto issue_v = [&](long long j, int row, int kvh) {
+        const int st = (int)(j % C::VST);
+        if (j >= C::VST) mbar_wait(&v_empty[st], (int)((j / C::VST) - 1) & 1, p.err);
+        uint8_t* vs = smem + C::kOffV + st * C::kKVBytes;
+        mbar_arrive_expect_tx(&v_full[st], C::kKVBytes);
+#pragma unroll
+        for (int pn = 0; pn < C::kPanels; ++pn)
+          tma_load_3d(vs + pn * C::kKVPanelBytes, &tm_v, &v_full[st], pn * 64, kvh, row);
+      };
       for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
@@ -402,24 +474,26 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           tma_load_3d(qs + pn * C::kQPanelBytes, &tm_q, &q_full[qb], pn * 64, ui.head, ui.q_row0);
         for (int t = 0; t < ui.n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
-          if (i >= C::ST) mbar_wait(&kv_empty[st], (int)((i / C::ST) - 1) & 1, p.err);
+          if (i >= C::ST) mbar_wait(&k_empty[st], (int)((i / C::ST) - 1) & 1, p.err);
           const int row = ui.kv_lo + t * C::BN;
           uint8_t* ks = smem + C::kOffK + st * C::kKVBytes;
-          uint8_t* vs = smem + C::kOffV + st * C::kKVBytes;
           mbar_arrive_expect_tx(&k_full[st], C::kKVBytes);
 #pragma unroll
           for (int pn = 0; pn < C::kPanels; ++pn)
             tma_load_3d(ks + pn * C::kKVPanelBytes, &tm_k, &k_full[st], pn * 64, ui.kv_head, row);
-          mbar_arrive_expect_tx(&v_full[st], C::kKVBytes);
-#pragma unroll
-          for (int pn = 0; pn < C::kPanels; ++pn)
-            tma_load_3d(vs + pn * C::kKVPanelBytes, &tm_v, &v_full[st], pn * 64, ui.kv_head, row);
+          if (v_pending) issue_v(i - 1, v_row, v_head);
+          v_pending = true;
+          v_row = row;
+          v_head = ui.kv_head;
         }
         ++lu;
       }
+      if (v_pending) issue_v(i - 1, v_row, v_head);
       // Tail: every commit that targets this CTA's barriers has landed before exit.
       for (long long j = (i > C::ST ? i - C::ST : 0); j < i; ++j)
-        mbar_wait(&kv_empty[j % C::ST], (int)(j / C::ST) & 1, p.err);
+        mbar_wait(&k_empty[j % C::ST], (int)(j / C::ST) & 1, p.err);
+      for (long long j = (i > C::VST ? i - C::VST : 0); j < i; ++j)
+        mbar_wait(&v_empty[j % C::VST], (int)(j / C::VST) & 1, p.err);
       for (int j = (lu > C::QB ? lu - C::QB : 0); j < lu; ++j) mbar_wait(&q_empty[j % C::QB], (j / C::QB) & 1, p.err);
     }
   } else if (warp == 1) {
@@ -434,9 +508,9 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       int prev_first = 0, prev_last = 0;
       auto issue_pv = [&](long long j, int first, int last) {
         const int sb = (int)(j % C::NS);
-        const int st = (int)(j % C::ST);
+        const int st = (int)(j % C::VST);
         mbar_wait(&p_full[sb], (int)(j / C::NS) & 1, p.err);
-        mbar_wait(&v_full[st], (int)(j / C::ST) & 1, p.err);
+        mbar_wait(&v_full[st], (int)(j / C::VST) & 1, p.err);
         tc_fence_after();
         const uint32_t v_addr = smem_base + C::kOffV + st * C::kKVBytes;
 #pragma unroll
@@ -445,7 +519,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           mma_ts(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
         }
         mma_commit(pv_done);
-        mma_commit(&kv_empty[st]);
+        mma_commit(&v_empty[st]);
         // One completion per unit: with two S buffers the next unit's QK is issued before this
         // P.V, so S-ready no longer implies earlier P.V completions; the epilogue needs its own.
         if (last) mma_commit(o_full);
@@ -454,6 +528,13 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
+        // The previous unit's last P.V goes first unless this unit's Q and first K are already
+        // resident: its epilogue must not wait on this unit's loads.
+        if (prev_i >= 0 &&
+            !(mbar_try_wait(&q_full[qb], (lu / C::QB) & 1) && mbar_try_wait(&k_full[i % C::ST], (int)(i / C::ST) & 1))) {
+          issue_pv(prev_i, prev_first, prev_last);
+          prev_i = -1;
+        }
         mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
         tc_fence_after();
         const uint32_t q_addr = smem_base + C::kOffQ + qb * C::kQBytes;
@@ -476,6 +557,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
             mma_ss(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[sb]);
+          mma_commit(&k_empty[st]);
           if (t == ui.n_kv - 1) mma_commit(&q_empty[qb]);
           if (prev_i >= 0) issue_pv(prev_i, prev_first, prev_last);
           prev_i = i;
@@ -510,7 +592,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     };
     long long i = 0;
     int lu = 0;
-    for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
+    for (ItemStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
       const UnitInfo ui = us.cur;
       if (ui.n_kv == 0) continue;
       // Allowed keys [klo, khi) of this row, in absolute key tokens.
@@ -685,20 +767,52 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
       __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head + half * kOCols;
-      constexpr int kEpi = (C::CPS == 1 && C::SPLIT == 1) ? 2 : 1;  // 32-column chunks per TMEM load
+      if constexpr (C::kStageOut) {
+        // 64 output columns per thread, in two 32-column halves: each half of all 32 rows of the
+        // warp goes through a 2 KB buffer (16-byte chunk c of row r at r*4 + (c ^ (r/2 % 4)),
+        // conflict-free both ways) and leaves as 64-byte row segments, 8 rows per instruction.
+        uint4* stage = reinterpret_cast<uint4*>(smem + C::kOffStage + sw * 2048);
 #pragma unroll
-      for (int cc = 0; cc < kOCols / 32; cc += kEpi) {
-        uint32_t o[kEpi * 32];
-        tmem_ld_chunks<kEpi>(o_addr + cc * 32, o);
-        tmem_wait_ld();
-        uint32_t pk[kEpi * 16];
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + hh * 32, o);
+          tmem_wait_ld();
+          uint32_t pk[16];
 #pragma unroll
-        for (int j = 0; j < kEpi * 16; ++j)
-          pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
-        if (store) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+          for (int j = 0; j < 16; ++j)
+            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
 #pragma unroll
-          for (int j = 0; j < kEpi * 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          for (int c = 0; c < 4; ++c)
+            stage[lane * 4 + (c ^ ((lane >> 1) & 3))] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int row = k * 8 + (lane >> 2), c = lane & 3;
+            const uint4 val = stage[row * 4 + (c ^ ((row >> 1) & 3))];
+            const int tr = quarter * 32 + row;  // tile row
+            const int tok = ui.q_row0 + tr;
+            if (tr < ui.nq && tok < p.total_q)
+              *reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)ui.head * p.o_head + half * kOCols +
+                                        hh * 32 + c * 8) = val;
+          }
+          __syncwarp();
+        }
+      } else {
+        constexpr int kEpi = (C::CPS == 1 && C::SPLIT == 1) ? 2 : 1;  // 32-column chunks per TMEM load
+#pragma unroll
+        for (int cc = 0; cc < kOCols / 32; cc += kEpi) {
+          uint32_t o[kEpi * 32];
+          tmem_ld_chunks<kEpi>(o_addr + cc * 32, o);
+          tmem_wait_ld();
+          uint32_t pk[kEpi * 16];
+#pragma unroll
+          for (int j = 0; j < kEpi * 16; ++j)
+            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+          if (store) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+            for (int j = 0; j < kEpi * 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          }
         }
       }
       if (store && half == 0 && p.lse != nullptr) {
@@ -1065,16 +1179,16 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
     case 64:
       // Layouts of the same kernel (PE_B200_D64_LAYOUT): default 64-key tiles, two S buffers and
       // two CTAs per SM; 2x1 / 1x2 are the 128-key-tile variants kept for comparison.
-      if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 2, 2, 1, 8>>(p, s, info.sms);
-      if (d64_layout() == 12) return launch_attention<Cfg<64, 128, 2, 2, 1, 2, 0>>(p, s, info.sms);
-      if (d64_layout() == 23) return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 0, 2>>(p, s, info.sms);
+      if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 3, 2, 2, 1, 8>>(p, s, info.sms);
+      if (d64_layout() == 12) return launch_attention<Cfg<64, 128, 2, 2, 2, 1, 2, 0>>(p, s, info.sms);
+      if (d64_layout() == 23) return launch_attention<Cfg<64, 64, 4, 4, 2, 2, 2, 0, 2>>(p, s, info.sms);
       switch (env_int("PE_B200_D64_POLY", 0)) {  // tuning knob: exp2 pairs (of 16) on the FMA pipe
-        case 4: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 4, 1>>(p, s, info.sms);
-        case 8: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 8, 1>>(p, s, info.sms);
-        default: return launch_attention<Cfg<64, 64, 4, 2, 2, 2, 0, 1>>(p, s, info.sms);
+        case 4: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 4, 1>>(p, s, info.sms);
+        case 8: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 8, 1>>(p, s, info.sms);
+        default: return launch_attention<Cfg<64, 64, 5, 3, 2, 2, 2, 0, 1>>(p, s, info.sms);
       }
-    case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 1, 4>>(p, s, info.sms);
-    case 256: return launch_attention<Cfg<256, 64, 2, 1, 2, 1, 0>>(p, s, info.sms);
+    case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4>>(p, s, info.sms);
+    case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0>>(p, s, info.sms);
     default: return PE_B200_ERR_UNSUPPORTED;
   }
 }
