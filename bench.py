@@ -335,6 +335,14 @@ def run_b200(args):
         record["cpu_baseline"] = cpu_baseline_record(args)
     if world == 1 and not args.no_extra:
         record["workloads"] = extra_workloads(pe, wl, peaks)
+        try:
+            record["comparators"] = comparators(pe, wl, record["workloads"])
+        except Exception as exc:  # noqa: BLE001
+            record["comparators"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
+        try:
+            record["config4_full_forward"] = config4_forward(pe)
+        except Exception as exc:  # noqa: BLE001
+            record["config4_full_forward"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
     print(json.dumps(record), flush=True)
     if world > 1:
         dist.barrier()
@@ -395,6 +403,136 @@ def extra_workloads(pe, wl, peaks, iters=10):
                      "hbm_gbs": round(gbs, 1), "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
                      "hbm_frac": round(gbs / peaks["hbm_gbs"], 4), "tokens": w.tokens}
         del q, k, v, out, plan
+    return res
+
+
+def _reference_importable():
+    """The reference package from its git-ignored install under baseline/_ref."""
+    for cand in (ROOT / "baseline" / "_ref",):
+        if (cand / "packed_encoders" / "__init__.py").exists():
+            if str(cand) not in sys.path:
+                sys.path.append(str(cand))
+            try:
+                import packed_encoders  # noqa: F401
+                return True
+            except Exception:  # noqa: BLE001
+                return False
+    return False
+
+
+def _time_call(fn, iters=10, flush=None):
+    times = []
+    for i in range(iters + 3):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(a.elapsed_time(b))
+    return statistics.median(times)
+
+
+def comparators(pe, wl, ours):
+    """The reference's own GPU kernels on the same box and inputs: its Triton packed-short
+    kernel (triton_packed_attention.py, inside its envelope: config 2) and FlashAttention-2
+    varlen (the compiled-FA path of ops.py:364-371; FA4 is not installed in this image)."""
+    out = {}
+    if not _reference_importable():
+        return {"unavailable": "reference package not importable (baseline/_ref missing)"}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    try:
+        from flash_attn import flash_attn_varlen_func
+    except Exception as exc:  # noqa: BLE001
+        flash_attn_varlen_func = None
+        out["fa2"] = f"unavailable: {type(exc).__name__}"
+    from packed_encoders._kernels.triton_packed_attention import packed_short_attention
+
+    cases = [("config1-global", wl.config1("global")), ("config1-local", wl.config1("local")),
+             ("config2-query-batch", wl.config2()), ("config3-global", wl.config3("global")),
+             ("config3-local", wl.config3("local")), ("config5-gqa-causal", wl.config5())]
+    for name, w in cases:
+        q, k, v = wl.make_qkv(w.lengths, w.heads, w.kv_heads, w.head_dim, seed=1)
+        cu = w.cu_seqlens().cuda()
+        (window, causal), = set(w.layers)
+        flops = wl.useful_flops(w.lengths, w.heads, w.head_dim, window, causal)
+        entry = {}
+        if flash_attn_varlen_func is not None:
+            try:
+                fn = lambda: flash_attn_varlen_func(q, k, v, cu, cu, max(w.lengths), max(w.lengths), dropout_p=0.0,
+                                                    softmax_scale=w.scale, causal=causal, window_size=window)
+                ms = _time_call(fn, flush=flush)
+                entry["fa2_ms"] = round(ms, 4)
+                entry["fa2_tflops"] = round(flops / (ms / 1e3) / 1e12, 2)
+            except Exception as exc:  # noqa: BLE001
+                entry["fa2"] = f"failed: {type(exc).__name__}: {str(exc)[:80]}"
+        if w.heads == 12 and w.head_dim == 64 and max(w.lengths) <= 128 and not causal:
+            half = None if window == (-1, -1) else window[0]
+            with torch.no_grad():
+                fn = lambda: packed_short_attention(q, k, v, cu, max(w.lengths), half_window=half,
+                                                    softmax_scale=w.scale)
+                ms = _time_call(fn, flush=flush)
+            entry["triton_ms"] = round(ms, 4)
+            entry["triton_tflops"] = round(flops / (ms / 1e3) / 1e12, 2)
+        if name in ours:
+            entry["b200_ms"] = ours[name]["ms"]
+            best = min(x for x in (entry.get("fa2_ms"), entry.get("triton_ms")) if x is not None) \
+                if ("fa2_ms" in entry or "triton_ms" in entry) else None
+            if best:
+                entry["speedup_vs_best_reference_kernel"] = round(best / ours[name]["ms"], 3)
+        out[name] = entry
+        del q, k, v
+    return out
+
+
+def config4_forward(pe):
+    """Config 4: a random-init ModernBERT-base packed_forward (22 layers, hidden 768, 12 heads,
+    GeGLU 1152, global every 3rd layer, RoPE theta 160000 / 10000) in bf16 on 256 queries
+    U[16,48] + 64 documents U[256,8192], through the reference's own forward with the b200
+    attention backend installed, against the same forward on its FlashAttention-2 path."""
+    if not _reference_importable():
+        return {"unavailable": "reference package not importable (baseline/_ref missing)"}
+    import packed_encoders as pe_ref
+    from packed_encoders import forward
+    from packed_encoders.arch.modernbert import ModernBert
+    from packed_encoders.config import ModernBertParams
+    from transformers import ModernBertConfig, ModernBertModel
+
+    from packed_encoders_b200 import install
+
+    install.install()
+    torch.manual_seed(0)
+    cfg = ModernBertConfig()
+    cfg._attn_implementation = "sdpa"
+    model = ModernBertModel(cfg).to("cuda", torch.bfloat16).eval()
+    pe_ref.pack(model, engine=ModernBert(pieces=install.b200_pieces()), attention_backend="b200", validate=False)
+    params = ModernBertParams.from_hf_config(model.config)
+    g = torch.Generator().manual_seed(0)
+    lengths = [int(x) for x in torch.randint(16, 49, (256,), generator=g)] + \
+              [int(x) for x in torch.randint(256, 8193, (64,), generator=g)]
+    cu = torch.tensor([0, *torch.tensor(lengths).cumsum(0).tolist()], dtype=torch.int32, device="cuda")
+    ids = torch.randint(1, cfg.vocab_size, (sum(lengths),), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    pos = torch.cat([torch.arange(n, device="cuda") for n in lengths])
+    res = {"tokens": sum(lengths), "sequences": len(lengths)}
+    from packed_encoders.arch.modernbert_pieces import default_execution
+
+    for backend in ("b200", "flash"):
+        # the FA2 run uses the reference's own pieces (its BSHD attention piece calls FA)
+        execution = None if backend == "b200" else default_execution()
+        try:
+            with torch.inference_mode():
+                fn = lambda: forward.packed_forward(model, params, ids, cu, max(lengths), pos, backend=backend,
+                                                    execution=execution)
+                ms = _time_call(fn, iters=5)
+            res[f"{backend}_ms"] = round(ms, 3)
+            res[f"{backend}_tokens_per_s"] = round(sum(lengths) / (ms / 1e3), 1)
+        except Exception as exc:  # noqa: BLE001
+            res[backend] = f"failed: {type(exc).__name__}: {str(exc)[:100]}"
+    if "b200_ms" in res and "flash_ms" in res:
+        res["speedup_vs_reference_fa2_forward"] = round(res["flash_ms"] / res["b200_ms"], 3)
+    del model
     return res
 
 

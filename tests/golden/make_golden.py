@@ -2,7 +2,7 @@
 
 Run in a container where the reference tree (packed-encoders 0.3.0) is importable:
 
-    PACKED_ENCODERS_CPU_CACHE_DIR= PYTHONPATH=/root/reference python tests/golden/make_golden.py
+    PACKED_ENCODERS_CPU_CACHE_DIR= PYTHONPATH=<reference checkout> python tests/golden/make_golden.py
 
 Every expected output below is produced by the REFERENCE's own code path, never by this
 repository's oracle:
@@ -133,7 +133,7 @@ if __name__ == "__main__":
     try:
         import packed_encoders  # noqa: F401
     except ImportError:
-        sys.exit("packed_encoders (the reference) must be importable: PYTHONPATH=/root/reference")
+        sys.exit("packed_encoders (the reference) must be importable: put its checkout on PYTHONPATH")
     torch.set_num_threads(4)
     with torch.inference_mode():
         native_cases()

@@ -1,7 +1,7 @@
 """The "b200" backend driven by the reference's own entry points (GPU).
 
-The reference package is imported from the git-ignored install in baseline/_ref (or the
-reference tree when mounted); the tests skip when neither exists. They mirror the
+The reference package is imported from its git-ignored install in baseline/_ref; the tests
+skip when it is absent. They mirror the
 reference's own GPU tests:
 
 * packed vs stock HF ModernBERT on padded batches, per-token cosine > 0.997
@@ -24,7 +24,7 @@ import torch
 import torch.nn.functional as F
 
 ROOT = Path(__file__).resolve().parents[1]
-for candidate in (ROOT / "baseline" / "_ref", Path("/root/reference")):
+for candidate in (ROOT / "baseline" / "_ref",):
     if (candidate / "packed_encoders" / "__init__.py").exists() and str(candidate) not in sys.path:
         sys.path.append(str(candidate))
         break
