@@ -448,7 +448,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // The whole warp runs the loop (uniform control flow); one elected lane issues each copy.
+    {
       long long i = 0;  // key tiles whose K is issued; V of tile i-1 follows K of tile i
       int lu = 0;
       int v_row = 0, v_head = 0;
@@ -457,10 +458,10 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         const int st = (int)(j % C::VST);
         if (j >= C::VST) mbar_wait(&v_empty[st], (int)((j / C::VST) - 1) & 1, p.err);
         uint8_t* vs = smem + C::kOffV + st * C::kKVBytes;
-        mbar_arrive_expect_tx(&v_full[st], C::kKVBytes);
+        mbar_arrive_expect_tx_w(&v_full[st], C::kKVBytes);
 #pragma unroll
         for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_load_3d(vs + pn * C::kKVPanelBytes, &tm_v, &v_full[st], pn * 64, kvh, row);
+          tma_load_3d_w(vs + pn * C::kKVPanelBytes, &tm_v, &v_full[st], pn * 64, kvh, row);
       };
       for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
@@ -468,19 +469,19 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         const int qb = lu % C::QB;
         if (lu >= C::QB) mbar_wait(&q_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
         uint8_t* qs = smem + C::kOffQ + qb * C::kQBytes;
-        mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
+        mbar_arrive_expect_tx_w(&q_full[qb], C::kQBytes);
 #pragma unroll
         for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_load_3d(qs + pn * C::kQPanelBytes, &tm_q, &q_full[qb], pn * 64, ui.head, ui.q_row0);
+          tma_load_3d_w(qs + pn * C::kQPanelBytes, &tm_q, &q_full[qb], pn * 64, ui.head, ui.q_row0);
         for (int t = 0; t < ui.n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
           if (i >= C::ST) mbar_wait(&k_empty[st], (int)((i / C::ST) - 1) & 1, p.err);
           const int row = ui.kv_lo + t * C::BN;
           uint8_t* ks = smem + C::kOffK + st * C::kKVBytes;
-          mbar_arrive_expect_tx(&k_full[st], C::kKVBytes);
+          mbar_arrive_expect_tx_w(&k_full[st], C::kKVBytes);
 #pragma unroll
           for (int pn = 0; pn < C::kPanels; ++pn)
-            tma_load_3d(ks + pn * C::kKVPanelBytes, &tm_k, &k_full[st], pn * 64, ui.kv_head, row);
+            tma_load_3d_w(ks + pn * C::kKVPanelBytes, &tm_k, &k_full[st], pn * 64, ui.kv_head, row);
           if (v_pending) issue_v(i - 1, v_row, v_head);
           v_pending = true;
           v_row = row;
@@ -498,7 +499,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop (uniform control flow); one elected lane issues each MMA.
+    {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileM, C::BN, false, false);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kTileM, C::D, false, true);
       const uint32_t smem_base = smem_u32(smem);
@@ -516,13 +518,13 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk) {
           const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
-          mma_ts(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
+          mma_ts_w(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
         }
-        mma_commit(pv_done);
-        mma_commit(&v_empty[st]);
+        mma_commit_w(pv_done);
+        mma_commit_w(&v_empty[st]);
         // One completion per unit: with two S buffers the next unit's QK is issued before this
         // P.V, so S-ready no longer implies earlier P.V completions; the epilogue needs its own.
-        if (last) mma_commit(o_full);
+        if (last) mma_commit_w(o_full);
       };
       for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
@@ -531,7 +533,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         // The previous unit's last P.V goes first unless this unit's Q and first K are already
         // resident: its epilogue must not wait on this unit's loads.
         if (prev_i >= 0 &&
-            !(mbar_try_wait(&q_full[qb], (lu / C::QB) & 1) && mbar_try_wait(&k_full[i % C::ST], (int)(i / C::ST) & 1))) {
+            !__all_sync(0xffffffffu, mbar_try_wait(&q_full[qb], (lu / C::QB) & 1) &&
+                                         mbar_try_wait(&k_full[i % C::ST], (int)(i / C::ST) & 1))) {
           issue_pv(prev_i, prev_first, prev_last);
           prev_i = -1;
         }
@@ -554,11 +557,11 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
             const uint32_t off = (kk & 3) * 32;
             const uint64_t adesc = sw128_desc(q_addr + (kk >> 2) * C::kQPanelBytes + off, 16, 1024);
             const uint64_t bdesc = sw128_desc(k_addr + (kk >> 2) * C::kKVPanelBytes + off, 16, 1024);
-            mma_ss(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+            mma_ss_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
           }
-          mma_commit(&s_full[sb]);
-          mma_commit(&k_empty[st]);
-          if (t == ui.n_kv - 1) mma_commit(&q_empty[qb]);
+          mma_commit_w(&s_full[sb]);
+          mma_commit_w(&k_empty[st]);
+          if (t == ui.n_kv - 1) mma_commit_w(&q_empty[qb]);
           if (prev_i >= 0) issue_pv(prev_i, prev_first, prev_last);
           prev_i = i;
           prev_first = (t == 0);
