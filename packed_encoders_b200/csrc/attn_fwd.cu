@@ -256,8 +256,8 @@ struct Cfg {
   static constexpr int kOffV = kOffK + ST * kKVBytes;
   static constexpr int kOffBar = kOffV + VST * kKVBytes;
   // barriers: k_full[ST] k_empty[ST] v_full[VST] v_empty[VST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS]
-  //           pv_done o_full
-  static constexpr int kNumBars = 2 * ST + 2 * VST + 2 * QB + 2 * NS + 2;
+  //           o_full
+  static constexpr int kNumBars = 2 * ST + 2 * VST + 2 * QB + 2 * NS + 1;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr int kOffXchg = kOffTmemSlot + 16;  // row max [2][SPLIT][128] and sum [SPLIT][128], fp32
   static constexpr int kXchgBytes = SPLIT > 1 ? 3 * SPLIT * kTileM * 4 : 0;
@@ -403,8 +403,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   uint64_t* q_empty = q_full + C::QB;
   uint64_t* s_full = q_empty + C::QB;
   uint64_t* p_full = s_full + C::NS;
-  uint64_t* pv_done = p_full + C::NS;  // every P.V (O rescale waits on the previous one)
-  uint64_t* o_full = pv_done + 1;       // the last P.V of each unit (epilogue)
+  uint64_t* o_full = p_full + C::NS;  // the last P.V of each unit (epilogue)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -427,7 +426,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4 * C::SPLIT);  // one arrival per softmax warp
     }
-    mbar_init(pv_done, 1);
     mbar_init(o_full, 1);
     fence_mbar_init();
   }
@@ -520,7 +518,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
           mma_ts_w(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
         }
-        mma_commit_w(pv_done);
         mma_commit_w(&v_empty[st]);
         // One completion per unit: with two S buffers the next unit's QK is issued before this
         // P.V, so S-ready no longer implies earlier P.V completions; the epilogue needs its own.
@@ -731,7 +728,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         // registers are free and the previous P.V has had the softmax time to finish.
         if (any_need) {
           // O holds the sum up to the previous key tile: wait for that P.V to land.
-          mbar_wait(pv_done, (int)((i - 1) & 1), p.err);
+          // (v_empty of that tile completes with it; its next phase needs this step's P.)
+          mbar_wait(&v_empty[(i - 1) % C::VST], (int)(((i - 1) / C::VST) & 1), p.err);
           tc_fence_after();
 #pragma unroll
           for (int cc = 0; cc < kOCols / 32; ++cc) {
