@@ -36,9 +36,10 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one attn_fwd_kernel launch (config 3 global
-# layer), from the ncu capture summarised in profiles/attn_fwd_config3.md; None until captured.
-NCU_TRAFFIC_GLOBAL = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one full-size attn_fwd_kernel launch (config 3
+# global layer, all 512 documents), from the one-pass ncu capture summarised in
+# profiles/attn_fwd_config3_global_traffic.md: 7.69 GB read + 0.914 GB written.
+NCU_TRAFFIC_GLOBAL = 7.69e9 + 0.914e9
 
 
 def _env_int(name, default):
@@ -317,6 +318,8 @@ def run_b200(args):
             "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4) if achieved else None,
             "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops burst)",
             "traffic": traffic,
+            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, full-size launch)",
+            "algorithmic_bytes": wl.algorithmic_bytes(my.tokens, my.tokens, heads, heads, dim),
             "avg_launch_ms": round(avg_kernel_ms, 4) if avg_kernel_ms else None,
             "launches": len(kernel_ms),
         },

@@ -35,6 +35,12 @@ namespace pe_b200 {
 
 constexpr int kTileM = 128;               // query rows per item / TMEM lanes
 constexpr int kHeaderBytes = 256;         // workspace header: n_items, error word
+// L2 policies of the TMA copies: Q tiles are read once (evict first); K/V tiles are re-read by
+// every query block of their sequence (0 normal, 1 evict last). Output rows are written with
+// streaming stores.
+constexpr bool kQEvictFirst = true;
+constexpr int kKVPolicy = 0;
+constexpr bool kStreamOut = true;
 constexpr int kCostBuckets = 1024;        // LPT ordering buckets (cost clamped)
 constexpr int kBuilderThreads = 1024;
 constexpr float kRescaleThreshold = 8.0f; // log2 units: rescale O only when the max grows > 2^8
@@ -99,14 +105,18 @@ __host__ __device__ __forceinline__ void block_key_range(int qb, int nq, int lq,
 
 __device__ __forceinline__ int cost_bucket(int cost) { return min(max(cost, 0), kCostBuckets - 1); }
 
-// Greedy walk over sequences [lo, hi): emits items in order through `emit(WorkItem)`.
+// Greedy walk over sequences [lo, hi): emits items in order through
+// `emit(item, index_in_group, group_size, group_cost)`. The query blocks of one long sequence
+// form a group that is placed contiguously in the schedule (ordered by the group's largest
+// item cost), so CTAs running at the same time share that sequence's K/V in L2; a packed
+// block of short sequences is a group of one.
 template <class Emit>
 __device__ void walk_sequences(const SchedParams& p, int lo, int hi, Emit emit) {
   int first = -1, count = 0, span_q = 0, span_k = 0;
   auto close = [&]() {
     if (first >= 0 && span_q > 0) {
       WorkItem it{first, count, 0, (span_k + p.block_n - 1) / p.block_n};
-      emit(it);
+      emit(it, 0, 1, it.cost);
     }
     first = -1;
     count = 0;
@@ -126,14 +136,16 @@ __device__ void walk_sequences(const SchedParams& p, int lo, int hi, Emit emit) 
     }
     if (lq > kTileM || lk > kTileM) {  // a long sequence: one item per 128-row query block
       close();
-      int nblk = (lq + kTileM - 1) / kTileM;
-      for (int qb = 0; qb < nblk; ++qb) {
-        int nq = min(kTileM, lq - qb * kTileM);
+      const int nblk = (lq + kTileM - 1) / kTileM;
+      auto item_of = [&](int qb) {
+        const int nq = min(kTileM, lq - qb * kTileM);
         int klo, khi;
         block_key_range(qb, nq, lq, lk, p.window_left, p.window_right, klo, khi);
-        WorkItem it{s, 1, qb, (khi - klo + p.block_n - 1) / p.block_n};
-        emit(it);
-      }
+        return WorkItem{s, 1, qb, (khi - klo + p.block_n - 1) / p.block_n};
+      };
+      int group_cost = 0;
+      for (int qb = 0; qb < nblk; ++qb) group_cost = max(group_cost, item_of(qb).cost);
+      for (int qb = 0; qb < nblk; ++qb) emit(item_of(qb), qb, nblk, group_cost);
       continue;
     }
     if (first >= 0 && span_q + lq <= kTileM && span_k + lk <= kTileM) {
@@ -206,7 +218,9 @@ __global__ void __launch_bounds__(kBuilderThreads) schedule_kernel(SchedParams p
   }
   const int chunk = (p.n_seq + blockDim.x - 1) / blockDim.x;
   const int lo = min(p.n_seq, tid * chunk), hi = min(p.n_seq, lo + chunk);
-  walk_sequences(p, lo, hi, [&](const WorkItem& it) { atomicAdd(&hist[cost_bucket(it.cost)], 1); });
+  walk_sequences(p, lo, hi, [&](const WorkItem&, int, int, int group_cost) {
+    atomicAdd(&hist[cost_bucket(group_cost)], 1);
+  });
   __syncthreads();
   int total = 0;
   for (int base = 0; base < kCostBuckets; base += blockDim.x) {  // blockDim == kCostBuckets
@@ -215,8 +229,10 @@ __global__ void __launch_bounds__(kBuilderThreads) schedule_kernel(SchedParams p
     if (b >= 0) cursor[b] = off;
   }
   __syncthreads();
-  walk_sequences(p, lo, hi, [&](const WorkItem& it) {
-    int pos = atomicAdd(&cursor[cost_bucket(it.cost)], 1);
+  int group_base = 0;
+  walk_sequences(p, lo, hi, [&](const WorkItem& it, int index, int group_size, int group_cost) {
+    if (index == 0) group_base = atomicAdd(&cursor[cost_bucket(group_cost)], group_size);
+    const int pos = group_base + index;
     if (pos < p.capacity) p.items[pos] = it;
   });
   if (tid == 0) {
@@ -276,6 +292,11 @@ struct Cfg {
   static_assert((BN / SPLIT) % 32 == 0 && (D / SPLIT) % 32 == 0 && SPLIT <= 2, "column split");
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
 };
+
+__device__ __forceinline__ void store_out(uint4* dst, uint4 v) {
+  if (kStreamOut) __stcs(dst, v);
+  else *dst = v;
+}
 
 struct UnitInfo {
   int head, kv_head;
@@ -448,6 +469,16 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     // ------------------------------------------------------------------ TMA producer
     // The whole warp runs the loop (uniform control flow); one elected lane issues each copy.
     {
+      const uint64_t pol_q = l2_policy_evict_first();
+      const uint64_t pol_kv = l2_policy_evict_last();
+      auto load_q = [&](void* dst, int c0, int c1, int c2, uint64_t* bar) {
+        if (kQEvictFirst) tma_load_3d_hint_w(dst, &tm_q, bar, c0, c1, c2, pol_q);
+        else tma_load_3d_w(dst, &tm_q, bar, c0, c1, c2);
+      };
+      auto load_kv = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+        if (kKVPolicy == 1) tma_load_3d_hint_w(dst, map, bar, c0, c1, c2, pol_kv);
+        else tma_load_3d_w(dst, map, bar, c0, c1, c2);
+      };
       long long i = 0;  // key tiles whose K is issued; V of tile i-1 follows K of tile i
       int lu = 0;
       int v_row = 0, v_head = 0;
@@ -459,7 +490,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         mbar_arrive_expect_tx_w(&v_full[st], C::kKVBytes);
 #pragma unroll
         for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_load_3d_w(vs + pn * C::kKVPanelBytes, &tm_v, &v_full[st], pn * 64, kvh, row);
+          load_kv(vs + pn * C::kKVPanelBytes, &tm_v, pn * 64, kvh, row, &v_full[st]);
       };
       for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
@@ -470,7 +501,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         mbar_arrive_expect_tx_w(&q_full[qb], C::kQBytes);
 #pragma unroll
         for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_load_3d_w(qs + pn * C::kQPanelBytes, &tm_q, &q_full[qb], pn * 64, ui.head, ui.q_row0);
+          load_q(qs + pn * C::kQPanelBytes, pn * 64, ui.head, ui.q_row0, &q_full[qb]);
         for (int t = 0; t < ui.n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
           if (i >= C::ST) mbar_wait(&k_empty[st], (int)((i / C::ST) - 1) & 1, p.err);
@@ -479,7 +510,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           mbar_arrive_expect_tx_w(&k_full[st], C::kKVBytes);
 #pragma unroll
           for (int pn = 0; pn < C::kPanels; ++pn)
-            tma_load_3d_w(ks + pn * C::kKVPanelBytes, &tm_k, &k_full[st], pn * 64, ui.kv_head, row);
+            load_kv(ks + pn * C::kKVPanelBytes, &tm_k, pn * 64, ui.kv_head, row, &k_full[st]);
           if (v_pending) issue_v(i - 1, v_row, v_head);
           v_pending = true;
           v_row = row;
@@ -793,8 +824,9 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
             const int tr = quarter * 32 + row;  // tile row
             const int tok = ui.q_row0 + tr;
             if (tr < ui.nq && tok < p.total_q)
-              *reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)ui.head * p.o_head + half * kOCols +
-                                        hh * 32 + c * 8) = val;
+              store_out(reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)ui.head * p.o_head +
+                                                 half * kOCols + hh * 32 + c * 8),
+                        val);
           }
           __syncwarp();
         }
@@ -812,7 +844,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           if (store) {
             uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
-            for (int j = 0; j < kEpi * 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            for (int j = 0; j < kEpi * 4; ++j) store_out(dst + j, make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]));
           }
         }
       }

@@ -162,3 +162,42 @@ def test_strided_v_view_like_modernbert():
                               cu.cuda(), 200, scale=0.125, window=(64, 64))
     ref, _ = oracle.attention(q, k, v, cu, scale=0.125, window=(64, 64))
     _assert_parity(out, ref, "strided v")
+
+
+@pytest.mark.parametrize("window,causal", [((-1, -1), False), ((64, 64), False), ((-1, -1), True)])
+def test_schedule_covers_every_block_once_with_sequences_contiguous(window, causal):
+    """The device tile schedule: every 128-row query block of every sequence appears exactly once;
+    the blocks of one long sequence are contiguous and in order (so concurrently running CTAs share
+    its K/V in L2); groups are ordered longest-first (LPT)."""
+    import packed_encoders_b200 as pe
+
+    lengths = [3000, 7, 129, 0, 40, 1000, 90, 2000, 1, 300, 64, 65, 500]
+    q, k, _, cu = packed_inputs(lengths, 2, 64, seed=5, device="cuda")
+    plan = pe.ops.plan_attention(q, k, cu, max(lengths), window=window, causal=causal)
+    torch.cuda.synchronize()
+    ws = plan.workspace.cpu().view(torch.int32)
+    n_items = int(ws[0])
+    items = ws[64:64 + 4 * n_items].view(-1, 4).tolist()  # header is 256 bytes
+    seen = {}
+    for pos, (first, count, qb, cost) in enumerate(items):
+        for s in range(first, first + count):
+            if count > 1:
+                assert lengths[s] <= 128
+            seen.setdefault(s, []).append((pos, qb))
+    for s, n in enumerate(lengths):
+        if n == 0:
+            continue
+        blocks = seen[s]
+        if n > 128:
+            assert [qb for _, qb in blocks] == list(range((n + 127) // 128))
+            positions = [pos for pos, _ in blocks]
+            assert positions == list(range(positions[0], positions[0] + len(positions)))
+        else:
+            assert len(blocks) == 1
+    group_cost = []
+    for first, count, qb, cost in items:
+        if qb == 0:
+            group_cost.append(cost)
+        else:
+            group_cost[-1] = max(group_cost[-1], cost)
+    assert group_cost == sorted(group_cost, reverse=True)
