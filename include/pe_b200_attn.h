@@ -98,6 +98,13 @@ int pe_b200_abi_version(void);
 /* Human-readable text for a status code. */
 const char* pe_b200_status_string(int status);
 
+/*
+ * The CUDA error behind the last PE_B200_ERR_CUDA returned on the calling host thread (which
+ * call failed and cudaGetErrorString of its error); "" if none. No counterpart in the
+ * reference (its kernels are launched by Triton / FlashAttention, which raise their own errors).
+ */
+const char* pe_b200_last_error_detail(void);
+
 /* 1 if `device` is an sm_100 part this library runs on, else 0. */
 int pe_b200_device_supported(int device);
 

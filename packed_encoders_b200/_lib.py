@@ -40,7 +40,7 @@ class PeB200AttnParams(ctypes.Structure):
 
 
 EXPORTS = (
-    "pe_b200_abi_version", "pe_b200_status_string", "pe_b200_device_supported",
+    "pe_b200_abi_version", "pe_b200_status_string", "pe_b200_last_error_detail", "pe_b200_device_supported",
     "pe_b200_attn_workspace_size", "pe_b200_attn_fwd", "pe_b200_build_schedule", "pe_b200_attn_run",
     "pe_b200_debug_qk", "pe_b200_debug_pv",
 )
@@ -61,6 +61,8 @@ def lib() -> ctypes.CDLL:
         raise PackedEncodersError("libpe_b200.so ABI version mismatch; rebuild it")
     so.pe_b200_status_string.restype = ctypes.c_char_p
     so.pe_b200_status_string.argtypes = [ctypes.c_int]
+    so.pe_b200_last_error_detail.restype = ctypes.c_char_p
+    so.pe_b200_last_error_detail.argtypes = []
     so.pe_b200_device_supported.restype = ctypes.c_int
     so.pe_b200_device_supported.argtypes = [ctypes.c_int]
     so.pe_b200_attn_workspace_size.restype = ctypes.c_int
@@ -82,4 +84,8 @@ def status_string(status: int) -> str:
 
 def check(status: int, what: str) -> None:
     if status != 0:
-        raise PackedEncodersError(f"{what} failed: {status_string(status)} (status {status})")
+        detail = ""
+        if status == -7:  # PE_B200_ERR_CUDA: name the CUDA call and its error
+            detail = lib().pe_b200_last_error_detail().decode()
+            detail = f" [{detail}]" if detail else ""
+        raise PackedEncodersError(f"{what} failed: {status_string(status)} (status {status}){detail}")

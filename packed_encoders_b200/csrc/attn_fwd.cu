@@ -25,6 +25,7 @@
 
 #include <cstdint>
 #include <cstdlib>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -257,10 +258,13 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
 //   SPLIT softmax warps per 32-row TMEM lane quarter, each owning 1/SPLIT of the key columns and
 //        of O (more warps to hide latency at the same registers per row).
-template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1>
+template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1, int PASS_ = 0>
 struct Cfg {
   static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_,
                        SPLIT = SPLIT_;
+  // S columns a softmax thread holds in registers at once (the row is re-read from TMEM for the
+  // exp pass when it is split into several passes).
+  static constexpr int kPass = PASS_ > 0 ? PASS_ : ((BN / SPLIT) < 64 ? BN / SPLIT : 64);
   static constexpr int kThreads = 64 + 128 * SPLIT;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
@@ -288,7 +292,7 @@ struct Cfg {
   // Hold a whole S row in registers only when the register budget allows it.
   static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
   static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
-  static_assert(BN % 64 == 0 && D % 64 == 0, "tile shape");
+  static_assert(BN % 32 == 0 && D % 64 == 0 && (BN / SPLIT) % kPass == 0 && kPass % 32 == 0, "tile shape");
   static_assert((BN / SPLIT) % 32 == 0 && (D / SPLIT) % 32 == 0 && SPLIT <= 2, "column split");
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
 };
@@ -605,7 +609,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     // [h*BN/SPLIT, (h+1)*BN/SPLIT) of every S tile and O columns [h*D/SPLIT, ...) of rows
     // 32*q'.. (q' = warp % 4); row maxima and sums are exchanged through shared memory.
     constexpr int kCols = C::BN / C::SPLIT;     // S columns per thread per key tile
-    constexpr int kPass = kCols < 64 ? kCols : 64;  // S columns held in registers at once
+    constexpr int kPass = C::kPass;  // S columns held in registers at once
     constexpr int kOCols = C::D / C::SPLIT;     // O columns per thread
     const int sw = warp - 2;
     const int half = sw >> 2;
@@ -864,6 +868,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   }
 }
 
+#include "attn_pair.cuh"
+
 // ---------------------------------------------------------------------------------------------
 // Layout probes: one CTA of 128 threads runs a single QK^T or P.V through the same descriptor
 // code as the kernel above.
@@ -1009,6 +1015,19 @@ static EncodeTiledFn encode_fn() {
 }
 
 // [tokens, heads, D] bf16 with element strides (token, head); box = 64 columns x 1 head x rows.
+// The CUDA error behind the last PE_B200_ERR_CUDA returned on this host thread.
+static thread_local char g_cuda_detail[192] = "";
+
+static int cuda_fail(const char* where, cudaError_t e) {
+  snprintf(g_cuda_detail, sizeof(g_cuda_detail), "%s: %s", where, cudaGetErrorString(e));
+  return PE_B200_ERR_CUDA;
+}
+
+static int launch_status(const char* where) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PE_B200_OK : cuda_fail(where, e);
+}
+
 static bool make_map(CUtensorMap* map, const void* base, long long tokens, int heads, int dim, long long tok_stride,
                      long long head_stride, int box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -1059,6 +1078,7 @@ static int d64_layout() {
     if (e && strcmp(e, "2x1") == 0) return 21;   // BN=128, two S buffers, one CTA per SM
     if (e && strcmp(e, "1x2") == 0) return 12;   // BN=128, one S buffer, two CTAs per SM
     if (e && strcmp(e, "split") == 0) return 23; // as the default with two softmax warps per row (column halves)
+    if (e && strcmp(e, "pair") == 0) return 31;  // two query tiles per CTA, 128-key tiles, shared K/V
     return 22;                                    // BN=64, two S buffers, two CTAs per SM, one warp per row
   }();
   return layout;
@@ -1104,14 +1124,14 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   if (!make_map(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
       !make_map(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
       !make_map(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN))
-    return PE_B200_ERR_CUDA;
+    return cuda_fail("tensor map encoding", cudaErrorInvalidValue);
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-        cudaSuccess)
-      return PE_B200_ERR_CUDA;
+    const cudaError_t e =
+        cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail("attn_fwd_kernel shared-memory attribute", e);
     attr_set[dev & 63] = true;
   }
   AttnParams ap;
@@ -1134,7 +1154,45 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
   attn_fwd_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
-  return cudaGetLastError() == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
+  return launch_status("attn_fwd_kernel launch");
+}
+
+template <class C>
+static int launch_pair(const PeB200AttnParams* p, cudaStream_t stream, int sms) {
+  CUtensorMap tq, tk, tv;
+  if (!make_map(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
+      !make_map(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
+      !make_map(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN))
+    return cuda_fail("tensor map encoding", cudaErrorInvalidValue);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(attn_pair_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail("attn_pair_kernel shared-memory attribute", e);
+    attr_set[dev & 63] = true;
+  }
+  AttnParams ap;
+  ap.cu_q = p->cu_seqlens_q;
+  ap.cu_k = p->cu_seqlens_k;
+  ap.heads = p->heads;
+  ap.group = p->heads / p->kv_heads;
+  ap.total_q = p->total_q;
+  ap.out = static_cast<__nv_bfloat16*>(p->out);
+  ap.o_tok = p->o_stride_token;
+  ap.o_head = p->o_stride_head;
+  ap.lse = p->lse;
+  ap.scale_log2 = p->scale * 1.4426950408889634f;
+  ap.window_left = p->window_left;
+  ap.window_right = p->causal ? 0 : p->window_right;
+  ap.header = static_cast<const WsHeader*>(p->workspace);
+  ap.items = reinterpret_cast<const WorkItem*>(static_cast<const uint8_t*>(p->workspace) + kHeaderBytes);
+  ap.err = &static_cast<WsHeader*>(p->workspace)->error;
+  const long long pairs = ((item_capacity(p) + 1) / 2) * p->heads;
+  const int grid = (int)(pairs < sms ? pairs : sms);
+  attn_pair_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
+  return launch_status("attn_pair_kernel launch");
 }
 
 }  // namespace pe_b200
@@ -1161,6 +1219,8 @@ const char* pe_b200_status_string(int status) {
     default: return "unknown status";
   }
 }
+
+const char* pe_b200_last_error_detail(void) { return g_cuda_detail; }
 
 int pe_b200_device_supported(int device) { return device_info(device).supported == 1 ? 1 : 0; }
 
@@ -1215,6 +1275,7 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
       if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 3, 2, 2, 1, 8>>(p, s, info.sms);
       if (d64_layout() == 12) return launch_attention<Cfg<64, 128, 2, 2, 2, 1, 2, 0>>(p, s, info.sms);
       if (d64_layout() == 23) return launch_attention<Cfg<64, 64, 4, 4, 2, 2, 2, 0, 2>>(p, s, info.sms);
+      if (d64_layout() == 31) return launch_pair<PairCfg<128, 4, 3, 2, 64>>(p, s, info.sms);
       switch (env_int("PE_B200_D64_POLY", 0)) {  // tuning knob: exp2 pairs (of 16) on the FMA pipe
         case 4: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 4, 1>>(p, s, info.sms);
         case 8: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 8, 1>>(p, s, info.sms);

@@ -201,3 +201,31 @@ def test_schedule_covers_every_block_once_with_sequences_contiguous(window, caus
         else:
             group_cost[-1] = max(group_cost[-1], cost)
     assert group_cost == sorted(group_cost, reverse=True)
+
+
+def test_pair_layout_matches_oracle_in_subprocess():
+    """The opt-in two-tiles-per-CTA layout (PE_B200_D64_LAYOUT=pair, read once per process) on
+    global, windowed, causal and packed-short cases."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    code = r"""
+import torch, oracle, packed_encoders_b200 as pe
+from conftest import packed_inputs
+for lengths, window, causal in [([300, 7, 129, 1000], (-1, -1), False), ([700, 40, 33, 260], (64, 64), False),
+                                ([513, 64, 65], (-1, -1), True), ([30] * 40 + [5, 100], (-1, -1), False)]:
+    q, k, v, cu = packed_inputs(lengths, 3, 64, seed=11)
+    out = pe.packed_attention(q.cuda(), k.cuda(), v.cuda(), cu.cuda(), max(lengths), scale=0.125, window=window,
+                              causal=causal)
+    ref, _ = oracle.attention(q.float(), k.float(), v.float(), cu, scale=0.125, window=window, causal=causal)
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, (lengths, window, causal, err)
+assert pe.device_error_word() == 0
+print("ok")
+"""
+    root = Path(__file__).resolve().parents[1]
+    env = dict(**__import__("os").environ, PE_B200_D64_LAYOUT="pair",
+               PYTHONPATH=f"{root}:{root / 'tests'}")
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+    assert res.returncode == 0 and "ok" in res.stdout, res.stderr[-2000:]
