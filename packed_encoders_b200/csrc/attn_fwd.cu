@@ -276,8 +276,8 @@ struct Cfg {
   static constexpr int kOffV = kOffK + ST * kKVBytes;
   static constexpr int kOffBar = kOffV + VST * kKVBytes;
   // barriers: k_full[ST] k_empty[ST] v_full[VST] v_empty[VST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS]
-  //           o_full
-  static constexpr int kNumBars = 2 * ST + 2 * VST + 2 * QB + 2 * NS + 1;
+  //           o_full row_empty[QB]
+  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr int kOffXchg = kOffTmemSlot + 16;  // row max [2][SPLIT][128] and sum [SPLIT][128], fp32
   static constexpr int kXchgBytes = SPLIT > 1 ? 3 * SPLIT * kTileM * 4 : 0;
@@ -286,12 +286,17 @@ struct Cfg {
   static constexpr bool kStageOut = (D / SPLIT) == 64 && CPS > 1;
   static constexpr int kOffStage = (kOffXchg + kXchgBytes + 127) & ~127;
   static constexpr int kStageBytes = kStageOut ? 4 * SPLIT * 2048 : 0;
-  static constexpr int kSmemBytes = kOffStage + kStageBytes + 1024;  // + align slack
+  // Per Q buffer: the unit's header (UnitInfo fields) and every row's allowed key interval,
+  // written by the producer so the softmax warps read no schedule data from global memory.
+  static constexpr int kRowSlotBytes = 64 + kTileM * 8;
+  static constexpr int kOffRows = kOffStage + kStageBytes;
+  static constexpr int kSmemBytes = kOffRows + QB * kRowSlotBytes + 1024;  // + align slack
   static constexpr uint32_t kColO = NS * BN;
   static constexpr uint32_t kTmemCols = (kColO + D <= 128) ? 128 : (kColO + D <= 256) ? 256 : 512;
   // Hold a whole S row in registers only when the register budget allows it.
   static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
   static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
   static_assert(BN % 32 == 0 && D % 64 == 0 && (BN / SPLIT) % kPass == 0 && kPass % 32 == 0, "tile shape");
   static_assert((BN / SPLIT) % 32 == 0 && (D / SPLIT) % 32 == 0 && SPLIT <= 2, "column split");
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
@@ -406,6 +411,52 @@ struct UnitStream {
   }
 };
 
+// Producer side of the row slot: the unit header and, for each of the 128 rows, the allowed
+// key interval [klo, khi) in absolute key tokens (rows past the unit get an empty interval).
+// Packed short sequences: the sequence of row tq is f + #(boundaries cu_q[f+1 .. f+c-1] <= tq),
+// counted with one coalesced load per 32 boundaries and warp shuffles.
+template <class C>
+__device__ __forceinline__ void write_row_slot(const AttnParams& p, const UnitInfo& ui, uint8_t* slot_bytes,
+                                               int lane) {
+  int* hdr = reinterpret_cast<int*>(slot_bytes);
+  int2* rows = reinterpret_cast<int2*>(hdr + 16);
+  if (lane == 0) {
+    hdr[0] = ui.q_row0;
+    hdr[1] = ui.nq;
+    hdr[2] = ui.head;
+    hdr[3] = ui.kv_lo;
+    hdr[4] = ui.n_kv;
+  }
+  int cnt[4] = {0, 0, 0, 0};
+  if (ui.c > 1) {
+    for (int base = 1; base < ui.c; base += 32) {
+      const int idx = base + lane;
+      const int v = idx < ui.c ? p.cu_q[ui.f + idx] : 0x7fffffff;
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j) {
+        const int b = __shfl_sync(0xffffffffu, v, j);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) cnt[g] += (b <= ui.q_row0 + lane + 32 * g) ? 1 : 0;
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int r = lane + 32 * g;
+    const int tq = ui.q_row0 + r;
+    int klo = 0, khi = 0;
+    if (r < ui.nq) {
+      const int s = min(ui.f + cnt[g], ui.f + ui.c - 1);
+      const int cq = p.cu_q[s], lq = p.cu_q[s + 1] - cq;
+      const int ck = p.cu_k[s], lk = p.cu_k[s + 1] - ck;
+      const int pos = tq - cq + (lk - lq);
+      klo = ck + (p.window_left >= 0 ? max(0, pos - p.window_left) : 0);
+      khi = ck + (p.window_right >= 0 ? min(lk, pos + p.window_right + 1) : lk);
+    }
+    rows[r] = make_int2(klo, khi);
+  }
+}
+
 // Load `n` consecutive 32-column chunks of this warp's TMEM lanes (no wait).
 template <int N>
 __device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[N * 32]) {
@@ -429,6 +480,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   uint64_t* s_full = q_empty + C::QB;
   uint64_t* p_full = s_full + C::NS;
   uint64_t* o_full = p_full + C::NS;  // the last P.V of each unit (epilogue)
+  uint64_t* row_empty = o_full + 1;    // [QB] the softmax warps took the unit's row slot
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -452,6 +504,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       mbar_init(&p_full[i], 4 * C::SPLIT);  // one arrival per softmax warp
     }
     mbar_init(o_full, 1);
+    for (int i = 0; i < C::QB; ++i) mbar_init(&row_empty[i], 4 * C::SPLIT);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -501,11 +554,17 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
         if (lu >= C::QB) mbar_wait(&q_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
+        // The Q copy goes first (its bytes are expected before the arrival), then the row slot;
+        // the producer's arrival on q_full, after the slot stores, publishes both.
         uint8_t* qs = smem + C::kOffQ + qb * C::kQBytes;
-        mbar_arrive_expect_tx_w(&q_full[qb], C::kQBytes);
+        mbar_expect_tx_w(&q_full[qb], C::kQBytes);
 #pragma unroll
         for (int pn = 0; pn < C::kPanels; ++pn)
           load_q(qs + pn * C::kQPanelBytes, pn * 64, ui.head, ui.q_row0, &q_full[qb]);
+        if (lu >= C::QB) mbar_wait(&row_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
+        write_row_slot<C>(p, ui, smem + C::kOffRows + qb * C::kRowSlotBytes, lane);
+        __syncwarp();  // the slot stores are ordered before the q_full arrival
+        if (lane == 0) mbar_arrive(&q_full[qb]);
         for (int t = 0; t < ui.n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
           if (i >= C::ST) mbar_wait(&k_empty[st], (int)((i / C::ST) - 1) & 1, p.err);
@@ -523,6 +582,16 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         ++lu;
       }
       if (v_pending) issue_v(i - 1, v_row, v_head);
+      {  // end marker for the softmax warps: a slot with n_kv = -1, published through q_full
+        const int qb = lu % C::QB;
+        if (lu >= C::QB) {
+          mbar_wait(&q_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
+          mbar_wait(&row_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
+        }
+        if (lane == 0) reinterpret_cast<int*>(smem + C::kOffRows + qb * C::kRowSlotBytes)[4] = -1;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[qb]);
+      }
       // Tail: every commit that targets this CTA's barriers has landed before exit.
       for (long long j = (i > C::ST ? i - C::ST : 0); j < i; ++j)
         mbar_wait(&k_empty[j % C::ST], (int)(j / C::ST) & 1, p.err);
@@ -627,33 +696,25 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     };
     long long i = 0;
     int lu = 0;
-    for (ItemStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
-      const UnitInfo ui = us.cur;
-      if (ui.n_kv == 0) continue;
-      // Allowed keys [klo, khi) of this row, in absolute key tokens.
+    for (;; ++lu) {
+      // The unit's header and this row's allowed keys [klo, khi) come from the producer's row
+      // slot, published with the unit's Q tile.
+      const int qb = lu % C::QB;
+      mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
+      const int* slot = reinterpret_cast<const int*>(smem + C::kOffRows + qb * C::kRowSlotBytes);
+      UnitInfo ui;
+      ui.q_row0 = slot[0];
+      ui.nq = slot[1];
+      ui.head = slot[2];
+      ui.kv_lo = slot[3];
+      ui.n_kv = slot[4];
+      if (ui.n_kv < 0) break;
+      const int2 kr = reinterpret_cast<const int2*>(slot + 16)[r];
+      const int klo = kr.x, khi = kr.y;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&row_empty[qb]);
       const bool row_valid = r < ui.nq;
       const int tq = ui.q_row0 + r;
-      int s = ui.f;
-      if (ui.c > 1) {
-        // Packed short sequences: my sequence is f + #(boundaries cu_q[f+1 .. f+c-1] <= tq),
-        // counted with one coalesced load per 32 boundaries and warp shuffles.
-        int cnt = 0;
-        for (int base = 1; base < ui.c; base += 32) {
-          const int idx = base + lane;
-          const int v = idx < ui.c ? p.cu_q[ui.f + idx] : 0x7fffffff;
-#pragma unroll 8
-          for (int j = 0; j < 32; ++j) cnt += (__shfl_sync(0xffffffffu, v, j) <= tq) ? 1 : 0;
-        }
-        s = min(ui.f + cnt, ui.f + ui.c - 1);
-      }
-      int klo = 0, khi = 0;
-      if (row_valid) {
-        const int cq = p.cu_q[s], lq = p.cu_q[s + 1] - cq;
-        const int ck = p.cu_k[s], lk = p.cu_k[s + 1] - ck;
-        const int pos = tq - cq + (lk - lq);
-        klo = ck + (p.window_left >= 0 ? max(0, pos - p.window_left) : 0);
-        khi = ck + (p.window_right >= 0 ? min(lk, pos + p.window_right + 1) : lk);
-      }
       float m_run = NEG_INF, l_run = 0.f;
       for (int t = 0; t < ui.n_kv; ++t, ++i) {
         const int sb = (int)(i % C::NS);
@@ -798,7 +859,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         l_run = l_all;
       }
       mbar_wait(o_full, lu & 1, p.err);
-      ++lu;
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row_valid && tq >= 0 && tq < p.total_q;

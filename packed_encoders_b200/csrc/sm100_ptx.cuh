@@ -137,6 +137,15 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 
+// Raise the barrier's expected transaction bytes without arriving (one elected lane).
+__device__ __forceinline__ void mbar_expect_tx_w(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;\n\t}\n" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx_w(uint64_t* bar, uint32_t bytes) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t.reg .b64 st;\n\telect.sync _|e, 0xffffffff;\n\t"
