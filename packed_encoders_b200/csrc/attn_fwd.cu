@@ -631,11 +631,9 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
-        // The previous unit's last P.V goes first unless this unit's Q and first K are already
-        // resident: its epilogue must not wait on this unit's loads.
-        if (prev_i >= 0 &&
-            !__all_sync(0xffffffffu, mbar_try_wait(&q_full[qb], (lu / C::QB) & 1) &&
-                                         mbar_try_wait(&k_full[i % C::ST], (int)(i / C::ST) & 1))) {
+        // The previous unit's last P.V goes before this unit's first QK: the softmax warps run
+        // that unit's epilogue before they can use the new S, so its O is what they wait for.
+        if (prev_i >= 0) {
           issue_pv(prev_i, prev_first, prev_last);
           prev_i = -1;
         }
