@@ -258,7 +258,8 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
 //   SPLIT softmax warps per 32-row TMEM lane quarter, each owning 1/SPLIT of the key columns and
 //        of O (more warps to hide latency at the same registers per row).
-template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1, int PASS_ = 0>
+template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1, int PASS_ = 0,
+          bool TMA_OUT_ = false>
 struct Cfg {
   static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_,
                        SPLIT = SPLIT_;
@@ -284,8 +285,14 @@ struct Cfg {
   // Epilogue staging (2 KB per softmax warp) so output rows leave as coalesced 128-byte lines;
   // only where shared memory allows (head_dim 64).
   static constexpr bool kStageOut = (D / SPLIT) == 64 && CPS > 1;
-  static constexpr int kOffStage = (kOffXchg + kXchgBytes + 127) & ~127;
-  static constexpr int kStageBytes = kStageOut ? 4 * SPLIT * 2048 : 0;
+  // TMA_OUT: with one warp per row, each warp's 32 staged rows leave through one TMA store (4 KB
+  // per warp, 128-byte swizzle: 16-byte chunk c of row r at r*128 + (c ^ r % 8)*16). Measured
+  // faster for windowed layers (config 3 local -9 %) and slower for global layers and query
+  // batches (+2 % / +5 %), so it is chosen per attention kind.
+  static constexpr bool kTmaOut = TMA_OUT_ && kStageOut && SPLIT == 1;
+  static constexpr int kStageAlign = kTmaOut ? 1024 : 128;  // the 128-byte swizzle needs 1 KB
+  static constexpr int kOffStage = (kOffXchg + kXchgBytes + kStageAlign - 1) & ~(kStageAlign - 1);
+  static constexpr int kStageBytes = kTmaOut ? 4 * 4096 : kStageOut ? 4 * SPLIT * 2048 : 0;
   // Per Q buffer: the unit's header (UnitInfo fields) and every row's allowed key interval,
   // written by the producer so the softmax warps read no schedule data from global memory.
   static constexpr int kRowSlotBytes = 64 + kTileM * 8;
@@ -467,7 +474,8 @@ __device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[N *
 template <class C>
 __global__ void __launch_bounds__(C::kThreads, C::CPS)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                    const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
@@ -861,11 +869,41 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
       __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head + half * kOCols;
-      if constexpr (C::kStageOut) {
+      if constexpr (C::kTmaOut) {
+        // The warp's 32 rows go to its 4 KB stage, then leave with one TMA store; a previous
+        // store from the stage must have finished reading it first.
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+      }
+      const bool tma_rows = C::kTmaOut && quarter * 32 + 32 <= ui.nq && ui.q_row0 + quarter * 32 + 32 <= p.total_q;
+      if (tma_rows) {
+        uint8_t* stage = smem + C::kOffStage + sw * 4096;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + hh * 32, o);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + (((hh * 4 + c) ^ (lane & 7)) * 16)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (kStreamOut) tma_store_3d_hint(&tm_o, stage, 0, ui.head, ui.q_row0 + quarter * 32, l2_policy_evict_first());
+          else tma_store_3d(&tm_o, stage, 0, ui.head, ui.q_row0 + quarter * 32);
+          bulk_commit_group();
+        }
+      } else if constexpr (C::kStageOut) {
         // 64 output columns per thread, in two 32-column halves: each half of all 32 rows of the
         // warp goes through a 2 KB buffer (16-byte chunk c of row r at r*4 + (c ^ (r/2 % 4)),
         // conflict-free both ways) and leaves as 64-byte row segments, 8 rows per instruction.
-        uint4* stage = reinterpret_cast<uint4*>(smem + C::kOffStage + sw * 2048);
+        uint4* stage = reinterpret_cast<uint4*>(smem + C::kOffStage + sw * (C::kTmaOut ? 4096 : 2048));
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t o[32];
@@ -916,6 +954,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       }
       tc_fence_before();
     }
+    if (C::kTmaOut && lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -1178,10 +1217,11 @@ static int validate(const PeB200AttnParams* p, int level) {
 
 template <class C>
 static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int sms) {
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   if (!make_map(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
       !make_map(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
-      !make_map(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN))
+      !make_map(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN) ||
+      !make_map(&to, p->out, p->total_q, p->heads, C::D, p->o_stride_token, p->o_stride_head, 32))
     return cuda_fail("tensor map encoding", cudaErrorInvalidValue);
   static bool attr_set[64] = {};
   int dev = 0;
@@ -1211,7 +1251,7 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   const long long units = item_capacity(p) * p->heads;
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
-  attn_fwd_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
+  attn_fwd_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, ap);
   return launch_status("attn_fwd_kernel launch");
 }
 
@@ -1337,7 +1377,10 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
       switch (env_int("PE_B200_D64_POLY", 0)) {  // tuning knob: exp2 pairs (of 16) on the FMA pipe
         case 4: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 4, 1>>(p, s, info.sms);
         case 8: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 8, 1>>(p, s, info.sms);
-        default: return launch_attention<Cfg<64, 64, 5, 3, 2, 2, 2, 0, 1>>(p, s, info.sms);
+        default:
+          if ((p->window_left >= 0 || p->window_right >= 0) && !p->causal)
+            return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1, 0, true>>(p, s, info.sms);
+          return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1>>(p, s, info.sms);
       }
     case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4>>(p, s, info.sms);
     case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0>>(p, s, info.sms);
