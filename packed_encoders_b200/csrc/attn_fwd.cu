@@ -730,24 +730,38 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         const int c_lo = klo - kt - col0, c_hi = khi - kt - col0;
         // Warp-uniform: every lane's row sees all my columns (interior tile), and which of my
         // 32-column chunks hold any allowed key of any lane of this warp.
+        // With the whole row in one pass, the S load is issued as soon as S is ready and the
+        // warp votes below run while it is in flight.
+        constexpr bool kEarlyLd = kCols == kPass;
+        uint32_t raw[kPass];
+        if (kEarlyLd) {
+          mbar_wait(&s_full[sb], (int)(i / C::NS) & 1, p.err);
+          tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < kPass / 32; ++cc)
+            tmem_ld32(s_addr + col0 + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+        }
         const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= kCols);
         uint32_t active = 0;
 #pragma unroll
         for (int cc = 0; cc < kCols / 32; ++cc)
           active |= (__any_sync(0xffffffffu, c_lo < 32 * (cc + 1) && c_hi > 32 * cc && c_lo < c_hi) ? 1u : 0u) << cc;
-        mbar_wait(&s_full[sb], (int)(i / C::NS) & 1, p.err);
-        tc_fence_after();
+        if (!kEarlyLd) {
+          mbar_wait(&s_full[sb], (int)(i / C::NS) & 1, p.err);
+          tc_fence_after();
+        }
 
         // ---- pass 1: row max of the raw scores (scale > 0 commutes with max); four
         // independent chains so the warp does not wait on its own latency.
-        uint32_t raw[kPass];
         float mxs[4] = {NEG_INF, NEG_INF, NEG_INF, NEG_INF};
 #pragma unroll
         for (int h = 0; h < kCols / kPass; ++h) {
+          if (!kEarlyLd) {
 #pragma unroll
-          for (int cc = 0; cc < kPass / 32; ++cc)
-            if (active & (1u << (h * (kPass / 32) + cc)))
-              tmem_ld32(s_addr + col0 + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+            for (int cc = 0; cc < kPass / 32; ++cc)
+              if (active & (1u << (h * (kPass / 32) + cc)))
+                tmem_ld32(s_addr + col0 + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+          }
           tmem_wait_ld();
           if (full) {
 #pragma unroll
