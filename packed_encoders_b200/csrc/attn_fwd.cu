@@ -878,9 +878,9 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         for (int o = 0; o < C::SPLIT; ++o) l_all += (o == half) ? l_run : xsum[o * kTileM + r];
         l_run = l_all;
       }
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       mbar_wait(o_full, lu & 1, p.err);
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
       __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head + half * kOCols;
       if constexpr (C::kTmaOut) {
@@ -892,11 +892,13 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       const bool tma_rows = C::kTmaOut && quarter * 32 + 32 <= ui.nq && ui.q_row0 + quarter * 32 + 32 <= p.total_q;
       if (tma_rows) {
         uint8_t* stage = smem + C::kOffStage + sw * 4096;
+        uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
+        tmem_ld32(o_addr, oo[0]);
+        tmem_ld32(o_addr + 32, oo[1]);
+        tmem_wait_ld();
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + hh * 32, o);
-          tmem_wait_ld();
+          const uint32_t* o = oo[hh];
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)
@@ -918,11 +920,13 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         // warp goes through a 2 KB buffer (16-byte chunk c of row r at r*4 + (c ^ (r/2 % 4)),
         // conflict-free both ways) and leaves as 64-byte row segments, 8 rows per instruction.
         uint4* stage = reinterpret_cast<uint4*>(smem + C::kOffStage + sw * (C::kTmaOut ? 4096 : 2048));
+        uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
+        tmem_ld32(o_addr, oo[0]);
+        tmem_ld32(o_addr + 32, oo[1]);
+        tmem_wait_ld();
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + hh * 32, o);
-          tmem_wait_ld();
+          const uint32_t* o = oo[hh];
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)
