@@ -540,6 +540,10 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         if (kQEvictFirst) tma_load_3d_hint_w(dst, &tm_q, bar, c0, c1, c2, pol_q);
         else tma_load_3d_w(dst, &tm_q, bar, c0, c1, c2);
       };
+      auto load_kv4 = [&](void* dst, const CUtensorMap* map, int row, int kvh, uint64_t* bar) {
+        if (kKVPolicy == 1) tma_load_4d_hint_w(dst, map, bar, 0, row, kvh, 0, pol_kv);
+        else tma_load_4d_w(dst, map, bar, 0, row, kvh, 0);
+      };
       auto load_kv = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
         if (kKVPolicy == 1) tma_load_3d_hint_w(dst, map, bar, c0, c1, c2, pol_kv);
         else tma_load_3d_w(dst, map, bar, c0, c1, c2);
@@ -553,9 +557,11 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         if (j >= C::VST) mbar_wait(&v_empty[st], (int)((j / C::VST) - 1) & 1, p.err);
         uint8_t* vs = smem + C::kOffV + st * C::kKVBytes;
         mbar_arrive_expect_tx_w(&v_full[st], C::kKVBytes);
-#pragma unroll
-        for (int pn = 0; pn < C::kPanels; ++pn)
-          load_kv(vs + pn * C::kKVPanelBytes, &tm_v, pn * 64, kvh, row, &v_full[st]);
+        if constexpr (C::kPanels > 1) {
+          load_kv4(vs, &tm_v, row, kvh, &v_full[st]);
+        } else {
+          load_kv(vs, &tm_v, 0, kvh, row, &v_full[st]);
+        }
       };
       for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
@@ -566,9 +572,12 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         // the producer's arrival on q_full, after the slot stores, publishes both.
         uint8_t* qs = smem + C::kOffQ + qb * C::kQBytes;
         mbar_expect_tx_w(&q_full[qb], C::kQBytes);
-#pragma unroll
-        for (int pn = 0; pn < C::kPanels; ++pn)
-          load_q(qs + pn * C::kQPanelBytes, pn * 64, ui.head, ui.q_row0, &q_full[qb]);
+        if constexpr (C::kPanels > 1) {
+          if (kQEvictFirst) tma_load_4d_hint_w(qs, &tm_q, &q_full[qb], 0, ui.q_row0, ui.head, 0, pol_q);
+          else tma_load_4d_w(qs, &tm_q, &q_full[qb], 0, ui.q_row0, ui.head, 0);
+        } else {
+          load_q(qs, 0, ui.head, ui.q_row0, &q_full[qb]);
+        }
         if (lu >= C::QB) mbar_wait(&row_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
         write_row_slot<C>(p, ui, smem + C::kOffRows + qb * C::kRowSlotBytes, lane);
         __syncwarp();  // the slot stores are ordered before the q_full arrival
@@ -579,9 +588,11 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           const int row = ui.kv_lo + t * C::BN;
           uint8_t* ks = smem + C::kOffK + st * C::kKVBytes;
           mbar_arrive_expect_tx_w(&k_full[st], C::kKVBytes);
-#pragma unroll
-          for (int pn = 0; pn < C::kPanels; ++pn)
-            load_kv(ks + pn * C::kKVPanelBytes, &tm_k, pn * 64, ui.kv_head, row, &k_full[st]);
+          if constexpr (C::kPanels > 1) {
+            load_kv4(ks, &tm_k, row, ui.kv_head, &k_full[st]);
+          } else {
+            load_kv(ks, &tm_k, 0, ui.kv_head, row, &k_full[st]);
+          }
           if (v_pending) issue_v(i - 1, v_row, v_head);
           v_pending = true;
           v_row = row;
@@ -630,10 +641,11 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
           mma_ts_w(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
         }
-        mma_commit_w(&v_empty[st]);
-        // One completion per unit: with two S buffers the next unit's QK is issued before this
-        // P.V, so S-ready no longer implies earlier P.V completions; the epilogue needs its own.
+        // One completion per unit (the epilogue waits on it, so it is committed first): with two
+        // S buffers the next unit's QK is issued before this P.V, so S-ready no longer implies
+        // earlier P.V completions.
         if (last) mma_commit_w(o_full);
+        mma_commit_w(&v_empty[st]);
       };
       for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
@@ -1157,6 +1169,24 @@ static bool make_map(CUtensorMap* map, const void* base, long long tokens, int h
   return r == CUDA_SUCCESS;
 }
 
+// Head dims above 64: a 4-D view {64 columns, tokens, heads, D/64 panels} (panel stride 128
+// bytes) so one copy brings every 64-column panel of a row block, landing panel-major
+// ([panel][row][128 B]) as the MMA descriptors expect.
+static bool make_map_panels(CUtensorMap* map, const void* base, long long tokens, int heads, int dim,
+                            long long tok_stride, long long head_stride, int box_rows) {
+  if (dim <= 64) return make_map(map, base, tokens, heads, dim, tok_stride, head_stride, box_rows);
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {64, (cuuint64_t)tokens, (cuuint64_t)heads, (cuuint64_t)(dim / 64)};
+  cuuint64_t strides[3] = {(cuuint64_t)tok_stride * 2, (cuuint64_t)head_stride * 2, 128};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, (cuuint32_t)(dim / 64)};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 struct DeviceInfo {
   int sms = 0;
   int supported = -1;
@@ -1236,9 +1266,9 @@ static int validate(const PeB200AttnParams* p, int level) {
 template <class C>
 static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int sms) {
   CUtensorMap tq, tk, tv, to;
-  if (!make_map(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
-      !make_map(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
-      !make_map(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN) ||
+  if (!make_map_panels(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
+      !make_map_panels(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
+      !make_map_panels(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN) ||
       !make_map(&to, p->out, p->total_q, p->heads, C::D, p->o_stride_token, p->o_stride_head, 32))
     return cuda_fail("tensor map encoding", cudaErrorInvalidValue);
   static bool attr_set[64] = {};

@@ -128,6 +128,26 @@ __device__ __forceinline__ void tma_load_3d_w(void* smem_dst, const CUtensorMap*
       : "memory");
 }
 
+// 4-D tiled load (one elected lane): all 64-column panels of a wide row block in one copy.
+__device__ __forceinline__ void tma_load_4d_w(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                              int c2, int c3) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];\n\t}\n" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_hint_w(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                                   int c1, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1, {%3, %4, %5, %6}], [%2], %7;\n\t}\n" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
+
 // As tma_load_3d_w with an L2 cache policy (createpolicy) for the copied lines.
 __device__ __forceinline__ void tma_load_3d_hint_w(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                                    int c1, int c2, uint64_t policy) {
