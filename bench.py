@@ -343,6 +343,10 @@ def run_b200(args):
         except Exception as exc:  # noqa: BLE001
             record["comparators"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
         try:
+            record["config5_output_gate"] = gate_fusion(pe, wl)
+        except Exception as exc:  # noqa: BLE001
+            record["config5_output_gate"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
+        try:
             record["config4_full_forward"] = config4_forward(pe)
         except Exception as exc:  # noqa: BLE001
             record["config4_full_forward"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
@@ -488,6 +492,44 @@ def comparators(pe, wl, ours):
         out[name] = entry
         del q, k, v
     return out
+
+
+def gate_fusion(pe, wl, iters=10):
+    """Config 5 with the Qwen3.5 output gate: the gate fused into the attention epilogue against
+    attention followed by the reference's own gate kernel (_kernels/hybrid.py:208-219, Triton)."""
+    w = wl.config5()
+    q, k, v = wl.make_qkv(w.lengths, w.heads, w.kv_heads, w.head_dim, seed=1)
+    gate = torch.randn(q.shape, device="cuda", generator=torch.Generator("cuda").manual_seed(7)).to(torch.bfloat16)
+    cu = w.cu_seqlens().cuda()
+    (window, causal), = set(w.layers)
+    plan = pe.ops.plan_attention(q, k, cu, max(w.lengths), window=window, causal=causal)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    kw = dict(scale=w.scale, window=window, causal=causal, plan=plan)
+    res = {}
+
+    def fused():
+        pe.packed_attention(q, k, v, cu, max(w.lengths), gate=gate, **kw)
+
+    res["fused_ms"] = round(_time_call(fused, iters, flush), 4)
+    ref_gate = None
+    if _reference_importable():
+        try:
+            from packed_encoders._kernels.hybrid import sigmoid_gate as ref_gate
+        except Exception as exc:  # noqa: BLE001
+            res["reference_gate_kernel"] = f"unavailable: {type(exc).__name__}"
+    if ref_gate is None:
+        def ref_gate(o, g):
+            return (o.float() * torch.sigmoid(g.float()).to(torch.bfloat16).float()).to(torch.bfloat16)
+        res["unfused_gate"] = "torch ops (reference gate kernel unavailable)"
+
+    def unfused():
+        o = pe.packed_attention(q, k, v, cu, max(w.lengths), **kw)
+        ref_gate(o, gate)
+
+    res["attention_then_gate_ms"] = round(_time_call(unfused, iters, flush), 4)
+    res["speedup"] = round(res["attention_then_gate_ms"] / res["fused_ms"], 3)
+    del q, k, v, gate, plan
+    return res
 
 
 def config4_forward(pe):

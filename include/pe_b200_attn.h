@@ -18,7 +18,7 @@
 extern "C" {
 #endif
 
-#define PE_B200_ABI_VERSION 1
+#define PE_B200_ABI_VERSION 2
 
 enum {
   PE_B200_OK = 0,
@@ -56,6 +56,11 @@ enum {
  * workspace: device memory of at least pe_b200_attn_workspace_size(...) bytes, 256-byte
  *   aligned. It holds the tile schedule and the device error word; its contents are
  *   rebuilt by every call, so one workspace serves calls on one stream in sequence.
+ * gate [total_q, heads, head_dim] bf16 (optional, NULL to skip), element strides
+ *   (g_stride_token, g_stride_head), D contiguous: out = bf16(o * bf16(sigmoid(gate))) with o
+ *   the bf16 attention output, the roundings of the reference's separate gate kernel
+ *   (packed_encoders/_kernels/hybrid.py:196-205, applied after attention at
+ *   packed_encoders/arch/qwen3_5/engine.py:570).
  *
  * Replaces (packed-encoders 0.3.0):
  *   packed_short_attention()      packed_encoders/_kernels/triton_packed_attention.py:175-236
@@ -90,6 +95,8 @@ typedef struct PeB200AttnParams {
   int32_t causal;
   void* workspace;
   size_t workspace_bytes;
+  const void* gate;
+  int64_t g_stride_token, g_stride_head;
 } PeB200AttnParams;
 
 /* ABI version of the loaded library (PE_B200_ABI_VERSION). */

@@ -88,6 +88,9 @@ struct AttnParams {
   const WsHeader* header;
   const WorkItem* items;
   int* err;
+  const __nv_bfloat16* gate;  // optional output gate [total_q, heads, D]
+  long long g_tok;
+  long long g_head;
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -259,8 +262,9 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //   SPLIT softmax warps per 32-row TMEM lane quarter, each owning 1/SPLIT of the key columns and
 //        of O (more warps to hide latency at the same registers per row).
 template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1, int PASS_ = 0,
-          bool TMA_OUT_ = false>
+          bool TMA_OUT_ = false, bool GATE_ = false>
 struct Cfg {
+  static constexpr bool kGate = GATE_;  // output gate fused into the epilogue (calls with a gate)
   static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_,
                        SPLIT = SPLIT_;
   // S columns a softmax thread holds in registers at once (the row is re-read from TMEM for the
@@ -312,6 +316,25 @@ struct Cfg {
 __device__ __forceinline__ void store_out(uint4* dst, uint4 v) {
   if (kStreamOut) __stcs(dst, v);
   else *dst = v;
+}
+
+// Output gate on 8 bf16 values: bf16(o * bf16(sigmoid(g))), the roundings of the reference's
+// separate gate kernel (packed_encoders/_kernels/hybrid.py:196-205).
+__device__ __forceinline__ uint4 gate8(uint4 o, uint4 g) {
+  const uint32_t ow[4] = {o.x, o.y, o.z, o.w}, gw[4] = {g.x, g.y, g.z, g.w};
+  uint32_t y[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float o0 = __uint_as_float(ow[w] << 16), o1 = __uint_as_float(ow[w] & 0xffff0000u);
+    const float g0 = __uint_as_float(gw[w] << 16), g1 = __uint_as_float(gw[w] & 0xffff0000u);
+    const uint32_t s = pack_bf16x2(__fdividef(1.f, 1.f + __expf(-g0)), __fdividef(1.f, 1.f + __expf(-g1)));
+    y[w] = pack_bf16x2(o0 * __uint_as_float(s << 16), o1 * __uint_as_float(s & 0xffff0000u));
+  }
+  return make_uint4(y[0], y[1], y[2], y[3]);
+}
+
+__device__ __forceinline__ uint4 load_gate8(const AttnParams& p, int tok, int head, int col) {
+  return __ldg(reinterpret_cast<const uint4*>(p.gate + (long long)tok * p.g_tok + (long long)head * p.g_head + col));
 }
 
 struct UnitInfo {
@@ -891,6 +914,16 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         l_run = l_all;
       }
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      // Gated calls (rows stored by their own thread): the first gate chunk is in flight while
+      // the last P.V completes.
+      constexpr int kGateChunk = (C::CPS == 1 && C::SPLIT == 1) ? 8 : 4;  // uint4 per 32*kEpi columns
+      uint4 g_next[(C::kGate && !C::kStageOut) ? kGateChunk : 1];
+      if constexpr (C::kGate && !C::kStageOut) {
+        if (row_valid && tq < p.total_q) {
+#pragma unroll
+          for (int j = 0; j < kGateChunk; ++j) g_next[j] = load_gate8(p, tq, ui.head, half * kOCols + j * 8);
+        }
+      }
       mbar_wait(o_full, lu & 1, p.err);
       tc_fence_after();
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
@@ -916,9 +949,11 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           for (int j = 0; j < 16; ++j)
             pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(stage + lane * 128 + (((hh * 4 + c) ^ (lane & 7)) * 16)) =
-                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          for (int c = 0; c < 4; ++c) {
+            uint4 val = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            if constexpr (C::kGate) val = gate8(val, load_gate8(p, tq, ui.head, hh * 32 + c * 8));
+            *reinterpret_cast<uint4*>(stage + lane * 128 + (((hh * 4 + c) ^ (lane & 7)) * 16)) = val;
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -950,18 +985,22 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int row = k * 8 + (lane >> 2), c = lane & 3;
-            const uint4 val = stage[row * 4 + (c ^ ((row >> 1) & 3))];
+            uint4 val = stage[row * 4 + (c ^ ((row >> 1) & 3))];
             const int tr = quarter * 32 + row;  // tile row
             const int tok = ui.q_row0 + tr;
-            if (tr < ui.nq && tok < p.total_q)
+            if (tr < ui.nq && tok < p.total_q) {
+              if constexpr (C::kGate) val = gate8(val, load_gate8(p, tok, ui.head, half * kOCols + hh * 32 + c * 8));
               store_out(reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)ui.head * p.o_head +
                                                  half * kOCols + hh * 32 + c * 8),
                         val);
+            }
           }
           __syncwarp();
         }
       } else {
         constexpr int kEpi = (C::CPS == 1 && C::SPLIT == 1) ? 2 : 1;  // 32-column chunks per TMEM load
+        // Gated calls: the gate of the next 32*kEpi columns is loaded while this chunk is finished.
+        static_assert(!C::kGate || kGateChunk == kEpi * 4, "gate chunk");
 #pragma unroll
         for (int cc = 0; cc < kOCols / 32; cc += kEpi) {
           uint32_t o[kEpi * 32];
@@ -973,8 +1012,22 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
             pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
           if (store) {
             uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+            uint4 g_cur[C::kGate ? kEpi * 4 : 1];
+            if constexpr (C::kGate) {
 #pragma unroll
-            for (int j = 0; j < kEpi * 4; ++j) store_out(dst + j, make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]));
+              for (int j = 0; j < kEpi * 4; ++j) g_cur[j] = g_next[j];
+              if (cc + kEpi < kOCols / 32) {
+#pragma unroll
+                for (int j = 0; j < kEpi * 4; ++j)
+                  g_next[j] = load_gate8(p, tq, ui.head, half * kOCols + (cc + kEpi) * 32 + j * 8);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < kEpi * 4; ++j) {
+              uint4 val = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+              if constexpr (C::kGate) val = gate8(val, g_cur[j]);
+              store_out(dst + j, val);
+            }
           }
         }
       }
@@ -1260,6 +1313,12 @@ static int validate(const PeB200AttnParams* p, int level) {
                               p->v_stride_token, p->v_stride_head, p->o_stride_token, p->o_stride_head};
   for (int64_t s : strides)
     if (s <= 0 || (s * 2) % 16 != 0) return PE_B200_ERR_STRIDE;
+  if (p->gate) {
+    if (!aligned16(p->gate)) return PE_B200_ERR_STRIDE;
+    if (p->g_stride_token <= 0 || p->g_stride_head <= 0 || (p->g_stride_token * 2) % 16 != 0 ||
+        (p->g_stride_head * 2) % 16 != 0)
+      return PE_B200_ERR_STRIDE;
+  }
   return PE_B200_OK;
 }
 
@@ -1296,6 +1355,9 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   ap.header = static_cast<const WsHeader*>(p->workspace);
   ap.items = reinterpret_cast<const WorkItem*>(static_cast<const uint8_t*>(p->workspace) + kHeaderBytes);
   ap.err = &static_cast<WsHeader*>(p->workspace)->error;
+  ap.gate = static_cast<const __nv_bfloat16*>(p->gate);
+  ap.g_tok = p->g_stride_token;
+  ap.g_head = p->g_stride_head;
   const long long units = item_capacity(p) * p->heads;
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
@@ -1335,6 +1397,9 @@ static int launch_pair(const PeB200AttnParams* p, cudaStream_t stream, int sms) 
   ap.header = static_cast<const WsHeader*>(p->workspace);
   ap.items = reinterpret_cast<const WorkItem*>(static_cast<const uint8_t*>(p->workspace) + kHeaderBytes);
   ap.err = &static_cast<WsHeader*>(p->workspace)->error;
+  ap.gate = static_cast<const __nv_bfloat16*>(p->gate);
+  ap.g_tok = p->g_stride_token;
+  ap.g_head = p->g_stride_head;
   const long long pairs = ((item_capacity(p) + 1) / 2) * p->heads;
   const int grid = (int)(pairs < sms ? pairs : sms);
   attn_pair_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
@@ -1414,6 +1479,14 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   const DeviceInfo& info = device_info(dev);
   if (info.supported != 1) return PE_B200_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->gate) {  // output gate fused: separate instantiations, so ungated kernels carry no gate code
+    switch (p->head_dim) {
+      case 64: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1, 0, false, true>>(p, s, info.sms);
+      case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4, 1, 0, false, true>>(p, s, info.sms);
+      case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 1, 0, false, true>>(p, s, info.sms);
+      default: return PE_B200_ERR_UNSUPPORTED;
+    }
+  }
   switch (p->head_dim) {
     case 64:
       // Layouts of the same kernel (PE_B200_D64_LAYOUT): default 64-key tiles, two S buffers and

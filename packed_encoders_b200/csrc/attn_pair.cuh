@@ -508,13 +508,14 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int row = k * 8 + (lane >> 2), c = lane & 3;
-          const uint4 val = stage[row * 4 + (c ^ ((row >> 1) & 3))];
+          uint4 val = stage[row * 4 + (c ^ ((row >> 1) & 3))];
           const int tr = quarter * 32 + row;
           const int tok = ui.q_row0 + tr;
-          if (tr < ui.nq && tok < p.total_q)
+          if (tr < ui.nq && tok < p.total_q) {
             store_out(reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)ui.head * p.o_head +
                                                hh * 32 + c * 8),
                       val);
+          }
         }
         __syncwarp();
       }

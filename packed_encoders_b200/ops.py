@@ -161,6 +161,7 @@ def packed_attention(
     out: Tensor | None = None,
     return_lse: bool = False,
     plan: AttentionPlan | None = None,
+    gate: Tensor | None = None,
 ):
     """Packed variable-length attention on B200.
 
@@ -171,6 +172,9 @@ def packed_attention(
     ``(left, right)`` with -1 unbounded (runtime/attention.py:157-170). Returns ``out``
     ``[Tq, H, D]`` bf16, and with ``return_lse`` also the fp32 natural-log LSE ``[H, Tq]``.
     ``plan`` (from ``plan_attention``) reuses an already built tile schedule.
+    ``gate`` ``[Tq, H, D]`` bf16 (D contiguous) fuses the Qwen3.5 output gate into the epilogue:
+    ``out = bf16(o * bf16(sigmoid(gate)))`` with ``o`` the bf16 attention output, the roundings
+    of the reference's ``sigmoid_gate`` (_kernels/hybrid.py:196-205); the LSE is not gated.
     """
     _check_qkv(q, k, v)
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
@@ -193,6 +197,9 @@ def packed_attention(
         out = torch.empty((tq, heads, dim), dtype=q.dtype, device=q.device)
     elif out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or out.device != q.device:
         raise UnsupportedTargetError("out must match q's shape/dtype with a contiguous head_dim")
+    if gate is not None and (gate.shape != q.shape or gate.dtype != torch.bfloat16 or gate.stride(2) != 1
+                             or gate.device != q.device):
+        raise UnsupportedTargetError("gate must be bf16 with q's shape and a contiguous head_dim")
     lse = torch.empty((heads, tq), dtype=torch.float32, device=q.device) if return_lse else None
     n_seq = cu_seqlens.numel() - 1
     if tq == 0 or n_seq == 0:
@@ -214,6 +221,9 @@ def packed_attention(
         scale=float(dim ** -0.5 if scale is None else scale),
         window_left=left, window_right=right, causal=int(bool(causal)),
     )
+    if gate is not None:
+        params.gate = _ptr(gate)
+        params.g_stride_token, params.g_stride_head = gate.stride(0), gate.stride(1)
     so = _lib.lib()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device)

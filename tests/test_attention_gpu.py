@@ -229,3 +229,27 @@ print("ok")
                PYTHONPATH=f"{root}:{root / 'tests'}")
     res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
     assert res.returncode == 0 and "ok" in res.stdout, res.stderr[-2000:]
+
+
+@pytest.mark.parametrize("dim,window,causal,heads,kv_heads", [
+    (64, (-1, -1), False, 4, 4), (64, (64, 64), False, 4, 4), (128, (-1, -1), True, 4, 2), (256, (-1, -1), True, 8, 2)])
+def test_output_gate_matches_unfused(dim, window, causal, heads, kv_heads):
+    """Fused output gate == attention then the reference's gate roundings:
+    bf16(o * bf16(sigmoid(g))) (packed_encoders/_kernels/hybrid.py:196-205). The gate is a strided
+    view, as when it comes out of a fused projection."""
+    import packed_encoders_b200 as pe
+
+    lengths = [300, 7, 129, 1000, 64, 1]
+    q, k, v, cu = packed_inputs(lengths, heads, dim, kv_heads=kv_heads, seed=3, device="cuda")
+    g_full = torch.randn(q.shape[0], heads, 2 * dim, device="cuda", generator=torch.Generator("cuda").manual_seed(4))
+    gate = (g_full * 3).to(torch.bfloat16)[:, :, dim:]
+    kw = dict(scale=dim ** -0.5, window=window, causal=causal)
+    plain = pe.packed_attention(q, k, v, cu, max(lengths), **kw)
+    fused = pe.packed_attention(q, k, v, cu, max(lengths), gate=gate, **kw)
+    ref = (plain.float() * torch.sigmoid(gate.float()).to(torch.bfloat16).float()).to(torch.bfloat16)
+    diff = (fused.float() - ref.float()).abs()
+    assert torch.isfinite(fused.float()).all()
+    # identical roundings; a sigmoid value within an ulp of a bf16 rounding boundary may round the other way
+    assert diff.max().item() <= 2e-2
+    assert (diff > 0).float().mean().item() < 0.01
+    assert pe.device_error_word() == 0

@@ -63,14 +63,31 @@ def test_workspace_size_and_validation():
     assert _size(_params(total_k=0))[0] == -2
 
 
-def test_struct_layout_matches_header():
-    # offsets of the C struct on x86-64 (pointers 8, int32 4, int64 8, natural alignment)
+def test_struct_layout_matches_header(tmp_path):
+    """The ctypes mirror has the C compiler's offsets for every field of PeB200AttnParams."""
     P = _lib.PeB200AttnParams
-    assert P.n_seq.offset == 56
-    assert P.q_stride_token.offset == 88
-    assert P.scale.offset == 152
-    assert P.workspace.offset == 168
-    assert ctypes.sizeof(P) == 184
+    names = [f[0] for f in P._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "pe_b200_attn.h"\nint main(void) {\n'
+                   + "".join(f'  printf("%zu\\n", offsetof(PeB200AttnParams, {n}));\n' for n in names)
+                   + '  printf("%zu\\n", sizeof(PeB200AttnParams));\n  return 0;\n}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    c_offsets = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                text=True).stdout.split()]
+    assert c_offsets[:-1] == [getattr(P, n).offset for n in names]
+    assert c_offsets[-1] == ctypes.sizeof(P)
+
+
+def test_gate_stride_validation_without_touching_cuda():
+    """A gate whose address or strides break the 16-byte rule is rejected before any CUDA call."""
+    base = dict(q=16, k=16, v=16, out=16, cu_seqlens_q=16, cu_seqlens_k=16, workspace=256, workspace_bytes=1 << 20,
+                q_stride_token=768, q_stride_head=64, k_stride_token=768, k_stride_head=64, v_stride_token=768,
+                v_stride_head=64, o_stride_token=768, o_stride_head=64)
+    so = _lib.lib()
+    assert so.pe_b200_attn_fwd(ctypes.byref(_params(**base, gate=24, g_stride_token=768, g_stride_head=64)), None) == -3
+    assert so.pe_b200_attn_fwd(ctypes.byref(_params(**base, gate=32, g_stride_token=770, g_stride_head=64)), None) == -3
+    assert so.pe_b200_attn_fwd(ctypes.byref(_params(**base, gate=32, g_stride_token=768, g_stride_head=0)), None) == -3
 
 
 def test_launch_entry_points_reject_null_workspace_without_touching_cuda():
