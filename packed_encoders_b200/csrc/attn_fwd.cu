@@ -255,7 +255,8 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //   D   head_dim;  BN key-tile rows;  ST / VST K / V ring stages (K is released after QK, V after
 //       P.V, and K runs one key tile ahead of V);  QB Q-tile buffers;
 //   NS  S buffers in TMEM (2: QK of the next key tile overlaps the softmax of this one;
-//       1: a single S, so two CTAs share an SM and overlap each other instead);
+//       3: QK runs two key tiles ahead of P.V, measured faster for windowed layers, whose units
+//       are a few key tiles long; 1: a single S, so two CTAs share an SM and overlap each other);
 //   CPS CTAs per SM the configuration is sized for (TMEM columns, shared memory, registers).
 //   POLY of every 16 exp2 pairs evaluated by a cubic on the FMA pipe instead of MUFU (MUFU is the
 //        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
@@ -650,8 +651,12 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       const uint32_t smem_base = smem_u32(smem);
       long long i = 0;
       int lu = 0;
-      long long prev_i = -1;
-      int prev_first = 0, prev_last = 0;
+      // P.V runs kLag key tiles behind QK: with a third S buffer the QK two tiles ahead is
+      // issued before this tile's P is ready, so S waits one more softmax step less often.
+      constexpr int kLag = C::NS >= 3 ? 2 : 1;
+      long long pend0 = 0;  // oldest key tile whose P.V is not issued yet (pending tiles are consecutive)
+      int npend = 0;
+      uint32_t pfirst = 0, plast = 0;  // bit k: pending tile pend0 + k is the first / last of its unit
       auto issue_pv = [&](long long j, int first, int last) {
         const int sb = (int)(j % C::NS);
         const int st = (int)(j % C::VST);
@@ -670,16 +675,20 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         if (last) mma_commit_w(o_full);
         mma_commit_w(&v_empty[st]);
       };
+      auto flush_one = [&]() {
+        issue_pv(pend0, (int)(pfirst & 1u), (int)(plast & 1u));
+        ++pend0;
+        --npend;
+        pfirst >>= 1;
+        plast >>= 1;
+      };
       for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
-        // The previous unit's last P.V goes before this unit's first QK: the softmax warps run
+        // The previous unit's last P.Vs go before this unit's first QK: the softmax warps run
         // that unit's epilogue before they can use the new S, so its O is what they wait for.
-        if (prev_i >= 0) {
-          issue_pv(prev_i, prev_first, prev_last);
-          prev_i = -1;
-        }
+        while (npend > 0) flush_one();
         mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
         tc_fence_after();
         const uint32_t q_addr = smem_base + C::kOffQ + qb * C::kQBytes;
@@ -687,10 +696,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           const int st = (int)(i % C::ST);
           const int sb = (int)(i % C::NS);
           // With one S buffer the previous P must be consumed first (issue order = execution order).
-          if (C::NS == 1 && prev_i >= 0) {
-            issue_pv(prev_i, prev_first, prev_last);
-            prev_i = -1;
-          }
+          if (C::NS == 1)
+            while (npend > 0) flush_one();
           mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
@@ -704,14 +711,15 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           mma_commit_w(&s_full[sb]);
           mma_commit_w(&k_empty[st]);
           if (t == ui.n_kv - 1) mma_commit_w(&q_empty[qb]);
-          if (prev_i >= 0) issue_pv(prev_i, prev_first, prev_last);
-          prev_i = i;
-          prev_first = (t == 0);
-          prev_last = (t == ui.n_kv - 1);
+          if (npend == 0) pend0 = i;
+          pfirst |= (t == 0 ? 1u : 0u) << npend;
+          plast |= (t == ui.n_kv - 1 ? 1u : 0u) << npend;
+          ++npend;
+          if (npend > kLag) flush_one();
         }
         ++lu;
       }
-      if (prev_i >= 0) issue_pv(prev_i, prev_first, prev_last);
+      while (npend > 0) flush_one();
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -1500,7 +1508,7 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
         case 8: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 8, 1>>(p, s, info.sms);
         default:
           if ((p->window_left >= 0 || p->window_right >= 0) && !p->causal)
-            return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1, 0, true>>(p, s, info.sms);
+            return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 1, 0, true>>(p, s, info.sms);
           return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1>>(p, s, info.sms);
       }
     case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4>>(p, s, info.sms);
