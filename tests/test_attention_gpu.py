@@ -225,8 +225,7 @@ assert pe.device_error_word() == 0
 print("ok")
 """
     root = Path(__file__).resolve().parents[1]
-    env = dict(**__import__("os").environ, PE_B200_D64_LAYOUT="pair",
-               PYTHONPATH=f"{root}:{root / 'tests'}")
+    env = {**__import__("os").environ, "PE_B200_D64_LAYOUT": "pair", "PYTHONPATH": f"{root}:{root / 'tests'}"}
     res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
     assert res.returncode == 0 and "ok" in res.stdout, res.stderr[-2000:]
 
