@@ -273,6 +273,9 @@ struct Cfg {
   static constexpr int kPass = PASS_ > 0 ? PASS_ : ((BN / SPLIT) < 64 ? BN / SPLIT : 64);
   static constexpr int kThreads = 64 + 128 * SPLIT;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
+  // Head dims above 64 issue their MMAs in groups of four from one elected lane (config 5,
+  // head_dim 256: -4 %); head_dim 64 keeps one elect per MMA (no measurable difference there).
+  static constexpr bool kGroupMma = D > 64;
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
   static constexpr int kKVPanelBytes = BN * 128;
   static constexpr int kQBytes = kPanels * kQPanelBytes;
@@ -309,7 +312,7 @@ struct Cfg {
   static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
   static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
-  static_assert(BN % 32 == 0 && D % 64 == 0 && (BN / SPLIT) % kPass == 0 && kPass % 32 == 0, "tile shape");
+  static_assert(BN % 64 == 0 && D % 64 == 0 && (BN / SPLIT) % kPass == 0 && kPass % 32 == 0, "tile shape");
   static_assert((BN / SPLIT) % 32 == 0 && (D / SPLIT) % 32 == 0 && SPLIT <= 2, "column split");
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
 };
@@ -664,10 +667,25 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         mbar_wait(&v_full[st], (int)(j / C::VST) & 1, p.err);
         tc_fence_after();
         const uint32_t v_addr = smem_base + C::kOffV + st * C::kKVBytes;
+        if constexpr (C::kGroupMma) {
 #pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk) {
-          const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
-          mma_ts_w(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
+          for (int g = 0; g < C::BN / 64; ++g) {  // groups of four 16-key k-steps
+            uint64_t bdesc[4];
+            uint32_t a_tm[4];
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              const int kk = g * 4 + k4;
+              bdesc[k4] = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
+              a_tm[k4] = tmem + C::col_s(sb) + kk * 8;
+            }
+            mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk) {
+            const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
+            mma_ts_w(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
+          }
         }
         // One completion per unit (the epilogue waits on it, so it is committed first): with two
         // S buffers the next unit's QK is issued before this P.V, so S-ready no longer implies
@@ -701,12 +719,25 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
+          if constexpr (C::kGroupMma) {
 #pragma unroll
-          for (int kk = 0; kk < C::D / 16; ++kk) {
-            const uint32_t off = (kk & 3) * 32;
-            const uint64_t adesc = sw128_desc(q_addr + (kk >> 2) * C::kQPanelBytes + off, 16, 1024);
-            const uint64_t bdesc = sw128_desc(k_addr + (kk >> 2) * C::kKVPanelBytes + off, 16, 1024);
-            mma_ss_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+            for (int g = 0; g < C::D / 64; ++g) {  // one 64-column panel: four 16-deep k-steps
+              uint64_t adesc[4], bdesc[4];
+#pragma unroll
+              for (int k4 = 0; k4 < 4; ++k4) {
+                adesc[k4] = sw128_desc(q_addr + g * C::kQPanelBytes + k4 * 32, 16, 1024);
+                bdesc[k4] = sw128_desc(k_addr + g * C::kKVPanelBytes + k4 * 32, 16, 1024);
+              }
+              mma_ss4_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, g > 0 ? 1u : 0u);
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < C::D / 16; ++kk) {
+              const uint32_t off = (kk & 3) * 32;
+              const uint64_t adesc = sw128_desc(q_addr + (kk >> 2) * C::kQPanelBytes + off, 16, 1024);
+              const uint64_t bdesc = sw128_desc(k_addr + (kk >> 2) * C::kKVPanelBytes + off, 16, 1024);
+              mma_ss_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+            }
           }
           mma_commit_w(&s_full[sb]);
           mma_commit_w(&k_empty[st]);

@@ -257,6 +257,32 @@ __device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint6
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
+// Four MMAs (the k-steps of one 64-deep slice) from one lane elected once for the group; the
+// first takes `accumulate`, the other three accumulate.
+__device__ __forceinline__ void mma_ss4_w(uint32_t d_tmem, const uint64_t (&a)[4], const uint64_t (&b)[4],
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e, t;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 t, %9, %9;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %10, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %10, t;\n\t}\n" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(accumulate),
+      "r"(idesc));
+}
+__device__ __forceinline__ void mma_ts4_w(uint32_t d_tmem, const uint32_t (&a_tmem)[4], const uint64_t (&b)[4],
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e, t;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 t, %9, %9;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %5, %10, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %6, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %10, t;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem[0]), "r"(a_tmem[1]), "r"(a_tmem[2]), "r"(a_tmem[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]),
+      "r"(accumulate), "r"(idesc));
+}
 __device__ __forceinline__ void mma_commit_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
