@@ -60,7 +60,9 @@ enum {
  *   (g_stride_token, g_stride_head), D contiguous: out = bf16(o * bf16(sigmoid(gate))) with o
  *   the bf16 attention output, the roundings of the reference's separate gate kernel
  *   (packed_encoders/_kernels/hybrid.py:196-205, applied after attention at
- *   packed_encoders/arch/qwen3_5/engine.py:570).
+ *   packed_encoders/arch/qwen3_5/engine.py:570). The library applies it with its own gate pass
+ *   on `stream` right after the attention kernel (or, with the environment variable
+ *   PE_B200_GATE=fused, inside the attention epilogue); both give the same bits.
  *
  * Replaces (packed-encoders 0.3.0):
  *   packed_short_attention()      packed_encoders/_kernels/triton_packed_attention.py:175-236

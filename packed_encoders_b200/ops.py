@@ -172,7 +172,7 @@ def packed_attention(
     ``(left, right)`` with -1 unbounded (runtime/attention.py:157-170). Returns ``out``
     ``[Tq, H, D]`` bf16, and with ``return_lse`` also the fp32 natural-log LSE ``[H, Tq]``.
     ``plan`` (from ``plan_attention``) reuses an already built tile schedule.
-    ``gate`` ``[Tq, H, D]`` bf16 (D contiguous) fuses the Qwen3.5 output gate into the epilogue:
+    ``gate`` ``[Tq, H, D]`` bf16 (D contiguous) applies the Qwen3.5 output gate in the same call:
     ``out = bf16(o * bf16(sigmoid(gate)))`` with ``o`` the bf16 attention output, the roundings
     of the reference's ``sigmoid_gate`` (_kernels/hybrid.py:196-205); the LSE is not gated.
     """

@@ -230,13 +230,16 @@ print("ok")
     assert res.returncode == 0 and "ok" in res.stdout, res.stderr[-2000:]
 
 
+@pytest.mark.parametrize("mode", ["pass", "fused"])
 @pytest.mark.parametrize("dim,window,causal,heads,kv_heads", [
     (64, (-1, -1), False, 4, 4), (64, (64, 64), False, 4, 4), (128, (-1, -1), True, 4, 2), (256, (-1, -1), True, 8, 2)])
-def test_output_gate_matches_unfused(dim, window, causal, heads, kv_heads):
-    """Fused output gate == attention then the reference's gate roundings:
-    bf16(o * bf16(sigmoid(g))) (packed_encoders/_kernels/hybrid.py:196-205). The gate is a strided
-    view, as when it comes out of a fused projection."""
+def test_output_gate_matches_unfused(dim, window, causal, heads, kv_heads, mode, monkeypatch):
+    """Output gate (the library's gate pass, and the fused epilogue) == attention then the
+    reference's gate roundings: bf16(o * bf16(sigmoid(g))) (packed_encoders/_kernels/hybrid.py:196-205).
+    The gate is a strided view, as when it comes out of a fused projection."""
     import packed_encoders_b200 as pe
+
+    monkeypatch.setenv("PE_B200_GATE", mode)
 
     lengths = [300, 7, 129, 1000, 64, 1]
     q, k, v, cu = packed_inputs(lengths, heads, dim, kv_heads=kv_heads, seed=3, device="cuda")
