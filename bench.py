@@ -195,7 +195,19 @@ def run_b200(args):
     device = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        # NCCL prints its version banner on stdout at communicator creation (when NCCL_DEBUG asks
+        # for it): send fd 1 to stderr meanwhile, so rank 0's stdout carries only the JSON line.
+        sys.stdout.flush()
+        saved_fd = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+            dist.barrier()
+        finally:
+            import ctypes
+            ctypes.CDLL(None).fflush(None)
+            os.dup2(saved_fd, 1)
+            os.close(saved_fd)
 
     layers = wl.config3("mix").layers
     lengths_all = wl.config3_lengths(512 * world, seed=0)
