@@ -255,3 +255,40 @@ def test_output_gate_matches_unfused(dim, window, causal, heads, kv_heads, mode,
     assert diff.max().item() <= 2e-2
     assert (diff > 0).float().mean().item() < 0.01
     assert pe.device_error_word() == 0
+
+
+def test_cuda_graph_capture_replays_new_lengths():
+    """Graph capture (the reference captures its packed forward, graph.py:8-18; no host syncs and
+    no host reads of cu_seqlens): a global and a windowed call captured once replay correctly after
+    new sequence lengths (same count and total) are written into the captured cu_seqlens buffer,
+    because the tile schedule is rebuilt on the device inside the graph."""
+    pe = _b200()
+    lengths_a, lengths_b = [300, 7, 129, 1000, 64], [100, 400, 1, 900, 99]
+    assert sum(lengths_a) == sum(lengths_b)
+    q, k, v, cu_a = packed_inputs(lengths_a, 4, 64, seed=21, device="cuda")
+    cu_b = torch.tensor([0] + lengths_b, dtype=torch.int32, device="cuda").cumsum(0, dtype=torch.int32)
+    cu = cu_a.clone()
+    bound = 1024  # a host-side upper bound on the lengths, as a graph runner passes
+    outs = [torch.empty_like(q), torch.empty_like(q)]
+    windows = [(-1, -1), (64, 64)]
+
+    def step():
+        for out, window in zip(outs, windows):
+            pe.packed_attention(q, k, v, cu, bound, scale=0.125, window=window, out=out)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()  # warm-up on the capture stream (its workspace is allocated here, not during capture)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step()
+    for new_cu in (cu_a, cu_b, cu_a):
+        cu.copy_(new_cu)
+        graph.replay()
+        torch.cuda.synchronize()
+        for out, window in zip(outs, windows):
+            eager = pe.packed_attention(q, k, v, new_cu, bound, scale=0.125, window=window)
+            assert torch.equal(out, eager), window
+    assert pe.device_error_word() == 0
