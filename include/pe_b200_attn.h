@@ -18,7 +18,7 @@
 extern "C" {
 #endif
 
-#define PE_B200_ABI_VERSION 2
+#define PE_B200_ABI_VERSION 3
 
 enum {
   PE_B200_OK = 0,
@@ -63,6 +63,14 @@ enum {
  *   packed_encoders/arch/qwen3_5/engine.py:570). The library applies it with its own gate pass
  *   on `stream` right after the attention kernel (or, with the environment variable
  *   PE_B200_GATE=fused, inside the attention epilogue); both give the same bits.
+ * rope_cos, rope_sin [total_q, head_dim] bf16 (optional, both or neither; row stride
+ *   rope_stride_token elements, D contiguous): q and k arrive un-rotated and the kernel applies
+ *   the rotary embedding to each Q and K tile in shared memory before its MMA, with the
+ *   reference's per-token tables and rotate-half rule (packed_encoders/_kernels/rope.py:5-6,
+ *   140-200: y_lo = x_lo*cos - x_hi*sin, y_hi = x_hi*cos + x_lo*sin in fp32, rounded to bf16),
+ *   replacing its separate apply_rope_bshd pass (packed_encoders/forward.py:199-205).
+ *   head_dim 64 and self-attention only (cu_seqlens_k == cu_seqlens_q, total_k == total_q);
+ *   other calls with tables return PE_B200_ERR_UNSUPPORTED.
  *
  * Replaces (packed-encoders 0.3.0):
  *   packed_short_attention()      packed_encoders/_kernels/triton_packed_attention.py:175-236
@@ -99,6 +107,9 @@ typedef struct PeB200AttnParams {
   size_t workspace_bytes;
   const void* gate;
   int64_t g_stride_token, g_stride_head;
+  const void* rope_cos; /* ABI 3: optional rotary tables, see above */
+  const void* rope_sin;
+  int64_t rope_stride_token;
 } PeB200AttnParams;
 
 /* ABI version of the loaded library (PE_B200_ABI_VERSION). */

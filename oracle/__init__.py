@@ -11,5 +11,6 @@ from oracle.oracle import (  # noqa: F401
     available_reference,
     build,
     reference_local_attention,
+    rope_bshd,
     useful_pairs,
 )

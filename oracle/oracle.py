@@ -172,3 +172,17 @@ def reference_local_attention(q, k, v, lengths, half, *, token_major=False, thre
     if status:
         raise ValueError(f"pe_local_attention failed: {status}")
     return out
+
+
+def rope_bshd(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotary embedding of ``x`` ``[T, H, D]`` with per-token tables ``[T, D]``, rotate-half
+    pairing (dims d and d + D/2), in fp32, rounded to ``x``'s dtype. Restates the reference's
+    ``t * cos + cat(-b, a) * sin`` (packed_encoders/cpu/attention.py:298-301) and its GPU
+    kernel's rounding of the result to the input dtype (packed_encoders/_kernels/rope.py:5-6,
+    190-197)."""
+    xf = x.float()
+    c = cos.float()[:, None, :]
+    s = sin.float()[:, None, :]
+    a, b = xf.chunk(2, -1)
+    return (xf * c + torch.cat((-b, a), -1) * s).to(x.dtype)
+

@@ -162,6 +162,7 @@ def packed_attention(
     return_lse: bool = False,
     plan: AttentionPlan | None = None,
     gate: Tensor | None = None,
+    rope: tuple[Tensor, Tensor] | None = None,
 ):
     """Packed variable-length attention on B200.
 
@@ -175,6 +176,11 @@ def packed_attention(
     ``gate`` ``[Tq, H, D]`` bf16 (D contiguous) applies the Qwen3.5 output gate in the same call:
     ``out = bf16(o * bf16(sigmoid(gate)))`` with ``o`` the bf16 attention output, the roundings
     of the reference's ``sigmoid_gate`` (_kernels/hybrid.py:196-205); the LSE is not gated.
+    ``rope`` ``(cos, sin)``, each ``[Tq, D]`` bf16 per-token tables (D contiguous, one row
+    stride): q and k are given un-rotated (e.g. views of the fused qkv projection) and the kernel
+    rotates each Q and K tile in shared memory, the reference's rotate-half rule of
+    ``apply_rope_bshd`` (_kernels/rope.py:140-200) fused into the attention instead of a pass of
+    its own (forward.py:199-205). head_dim 64, self-attention (no ``cu_seqlens_k``) only.
     """
     _check_qkv(q, k, v)
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
@@ -197,6 +203,14 @@ def packed_attention(
         out = torch.empty((tq, heads, dim), dtype=q.dtype, device=q.device)
     elif out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or out.device != q.device:
         raise UnsupportedTargetError("out must match q's shape/dtype with a contiguous head_dim")
+    if rope is not None:
+        cos, sin = rope
+        if (cos.shape != (tq, dim) or sin.shape != cos.shape or cos.dtype != torch.bfloat16
+                or sin.dtype != torch.bfloat16 or cos.stride(1) != 1 or sin.stride(1) != 1
+                or cos.stride(0) != sin.stride(0) or cos.device != q.device or sin.device != q.device):
+            raise UnsupportedTargetError("rope tables must be bf16 [Tq, D] with a contiguous D and one row stride")
+        if dim != 64 or cu_seqlens_k is not None or tk != tq:
+            raise UnsupportedTargetError("fused rope: head_dim 64 self-attention only")
     if gate is not None and (gate.shape != q.shape or gate.dtype != torch.bfloat16 or gate.stride(2) != 1
                              or gate.device != q.device):
         raise UnsupportedTargetError("gate must be bf16 with q's shape and a contiguous head_dim")
@@ -224,6 +238,9 @@ def packed_attention(
     if gate is not None:
         params.gate = _ptr(gate)
         params.g_stride_token, params.g_stride_head = gate.stride(0), gate.stride(1)
+    if rope is not None:
+        params.rope_cos, params.rope_sin = _ptr(rope[0]), _ptr(rope[1])
+        params.rope_stride_token = rope[0].stride(0)
     so = _lib.lib()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device)

@@ -30,7 +30,24 @@ def pytest_collection_modifyitems(config, items):
 
 
 def golden_names() -> list[str]:
-    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+    """Plain attention fixtures (the ``rope_*`` ones take un-rotated q/k plus tables)."""
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("rope_"))
+
+
+def rope_golden_names() -> list[str]:
+    return sorted(p.stem for p in GOLDEN.glob("rope_*.npz"))
+
+
+def load_rope_golden(name: str) -> dict:
+    """A ``rope_*`` fixture: un-rotated q/k/v, bf16 per-token tables, the reference's rotated q/k
+    (fp32) and its attention output over them."""
+    g = load_golden(name)
+    data = np.load(GOLDEN / f"{name}.npz")
+    for key in ("cos", "sin"):
+        g[key] = torch.from_numpy(data[key].view(np.int16).copy()).view(torch.bfloat16)
+    g["rq"] = torch.from_numpy(data["rq"].copy())
+    g["rk"] = torch.from_numpy(data["rk"].copy())
+    return g
 
 
 def load_golden(name: str) -> dict:
@@ -60,3 +77,14 @@ def packed_inputs(lengths, heads, dim, *, kv_heads=None, seed=0, device="cpu", l
     if len(lengths):
         cu[1:] = torch.tensor(list(lengths), dtype=torch.int64).cumsum(0).to(torch.int32)
     return q.to(device), k.to(device), v.to(device), cu.to(device)
+
+
+def rope_tables(lengths, theta=10000.0, dim=64, device="cpu"):
+    """Per-token gathered RoPE tables [T, dim] bf16 (positions restart in every sequence), the
+    rotary embedding of ModernBERT (inverse frequencies theta^(-2i/dim), emb = [freqs, freqs])."""
+    inv = 1.0 / theta ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim)
+    pos = torch.cat([torch.arange(int(n), dtype=torch.float32) for n in lengths])
+    freqs = pos[:, None] * inv[None, :]
+    emb = torch.cat((freqs, freqs), -1)
+    return emb.cos().to(torch.bfloat16).to(device), emb.sin().to(torch.bfloat16).to(device)
+

@@ -16,6 +16,8 @@ repository's oracle:
   Qwen3.5 attention geometry 8/2/256 (tests/test_qwen35.py:136-152).
 - ``prefixed_*``: ``runtime.attention.reference_prefixed`` (runtime/attention.py:242-244)
   on the prefixed probe lengths of runtime/attention.py:250.
+- ``rope_*``: ``CPUAttention.rope_layout`` (cpu/attention.py:281-303) then ``_native``: RoPE'd
+  attention from un-rotated q/k and per-token tables (see ``rope_cases``).
 
 The reference returns no log-sum-exp, so the fixtures carry none; LSE is checked against
 the oracle's definition (natural log of the softmax denominator) in the tests.
@@ -129,12 +131,66 @@ def segment_cases():
           window=(-1, -1), causal=True, note="runtime/attention.py:250 prefixed probe lengths")
 
 
+def rope_tables(lengths, theta, dim=64):
+    """Per-token gathered RoPE tables [T, dim] (positions restart at 0 in every sequence;
+    ModernBERT's rotary embedding: inverse frequencies theta^(-2i/dim), emb = [freqs, freqs])."""
+    inv = 1.0 / theta ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim)
+    pos = torch.cat([torch.arange(n, dtype=torch.float32) for n in lengths])
+    freqs = pos[:, None] * inv[None, :]
+    emb = torch.cat((freqs, freqs), -1)
+    return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+
+
+def rope_cases():
+    """``rope_*``: the reference's CPU RoPE (``CPUAttention.rope_layout``, cpu/attention.py:281-303,
+    rotate-half in fp32) on un-rotated q/k from a packed qkv, then its native attention on the
+    rotated q/k. The fixtures keep q/k un-rotated plus the bf16 tables, the reference's rotated q/k
+    (fp32) and its attention output."""
+    from packed_encoders.cpu.attention import CPUAttention
+
+    engine = CPUAttention("native", 64, 64, 4)
+    if engine.library is None:
+        raise SystemExit("reference native CPU attention did not build")
+
+    def run(name, lengths, heads, half, theta, seed, note):
+        gen = torch.Generator().manual_seed(seed)
+        total = sum(lengths)
+        q, k, v = (_bf16((total, heads, 64), gen) for _ in range(3))
+        cos, sin = rope_tables(lengths, theta)
+        qkv = torch.stack((q, k, v), 1).float().reshape(1, total, 3 * heads * 64).contiguous()
+        rq, rk, rv = (t.clone().contiguous() for t in
+                      engine.rope_layout(qkv, cos.float()[None, None].contiguous(), sin.float()[None, None].contiguous(),
+                                         heads, 64))
+        boundaries = torch.tensor(lengths, dtype=torch.int32)
+        out = engine._native(rq, rk, rv, tuple(lengths), boundaries, half).clone()
+        out = out.squeeze(0).permute(1, 0, 2).contiguous()
+        window = (-1, -1) if half >= max(lengths) else (half, half)
+        path = HERE / f"{name}.npz"
+        np.savez_compressed(
+            path, q=_bits(q), k=_bits(k), v=_bits(v), cos=_bits(cos), sin=_bits(sin), cu_q=_cu(lengths),
+            cu_k=_cu(lengths), out=out.to(torch.float32).numpy(),
+            rq=rq.squeeze(0).permute(1, 0, 2).contiguous().numpy(), rk=rk.squeeze(0).permute(1, 0, 2).contiguous().numpy(),
+            scale=np.float32(0.125), window=np.array(window, dtype=np.int32), causal=np.int32(0), note=np.array(note),
+        )
+        print(f"{path.name}: T={total} H={heads} window={window} theta={theta} bytes={path.stat().st_size}")
+
+    run("rope_native_local", [7, 65, 66, 1, 130, 200], 1, 64, 10000.0, 6,
+        "test_modernbert_cpu.py:302-321 lengths; local layers, RoPE theta 10000")
+    run("rope_native_global", [17, 1, 8, 3, 65, 2, 128, 300], 1, 300, 160000.0, 7,
+        "test_modernbert_cpu.py:527-551 lengths + 300; global layers, RoPE theta 160000")
+
+
 if __name__ == "__main__":
     try:
         import packed_encoders  # noqa: F401
     except ImportError:
         sys.exit("packed_encoders (the reference) must be importable: put its checkout on PYTHONPATH")
     torch.set_num_threads(4)
+    only = sys.argv[1:]
     with torch.inference_mode():
-        native_cases()
-        segment_cases()
+        if not only or "native" in only:
+            native_cases()
+        if not only or "segments" in only:
+            segment_cases()
+        if not only or "rope" in only:
+            rope_cases()

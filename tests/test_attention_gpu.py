@@ -11,7 +11,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import golden_names, load_golden, packed_inputs
+from conftest import golden_names, load_golden, load_rope_golden, packed_inputs, rope_golden_names, rope_tables
 
 pytestmark = pytest.mark.gpu
 
@@ -292,3 +292,67 @@ def test_cuda_graph_capture_replays_new_lengths():
             eager = pe.packed_attention(q, k, v, new_cu, bound, scale=0.125, window=window)
             assert torch.equal(out, eager), window
     assert pe.device_error_word() == 0
+
+
+@pytest.mark.parametrize("name", rope_golden_names())
+def test_rope_golden_vectors(name):
+    """Fused RoPE against the reference's own pipeline: its CPU RoPE (cpu/attention.py:281-303)
+    on un-rotated q/k, then its native attention (fixtures from tests/golden/make_golden.py)."""
+    pe = _b200()
+    g = load_rope_golden(name)
+    lengths = (g["cu_q"][1:] - g["cu_q"][:-1]).tolist()
+    out = pe.packed_attention(g["q"].cuda(), g["k"].cuda(), g["v"].cuda(), g["cu_q"].cuda(), max(lengths),
+                              scale=g["scale"], window=g["window"], rope=(g["cos"].cuda(), g["sin"].cuda()))
+    torch.cuda.synchronize()
+    _assert_parity(out, g["out"], name)
+    assert pe.device_error_word() == 0
+
+
+ROPE_CASES = [
+    # (lengths, heads, kv_heads, window, causal)
+    ([300, 7, 129, 1000, 64, 1], 4, 4, (-1, -1), False),
+    ([300, 7, 129, 1000, 64, 1], 4, 4, (64, 64), False),
+    ([30] * 40 + [5, 100], 12, 12, (-1, -1), False),
+    ([700, 3, 260], 4, 2, (-1, -1), True),
+    ([17, 250, 9, 0, 128], 4, 1, (16, 3), False),
+]
+
+
+@pytest.mark.parametrize("lengths,heads,kv_heads,window,causal", ROPE_CASES)
+def test_fused_rope_matches_rotate_then_attend(lengths, heads, kv_heads, window, causal):
+    """Fused RoPE == the oracle's rotation of q and k followed by attention (parity bars), and ==
+    this library's unfused path on the same rotated inputs up to rare last-bit differences of the
+    rotation's rounding."""
+    pe = _b200()
+    q, k, v, cu = packed_inputs(lengths, heads, 64, kv_heads=kv_heads, seed=31)
+    cos, sin = rope_tables(lengths, theta=160000.0 if window == (-1, -1) else 10000.0)
+    rq, rk = oracle.rope_bshd(q, cos, sin), oracle.rope_bshd(k, cos, sin)
+    ref, _ = oracle.attention(rq, rk, v, cu, scale=0.125, window=window, causal=causal)
+    kw = dict(scale=0.125, window=window, causal=causal)
+    out = pe.packed_attention(q.cuda(), k.cuda(), v.cuda(), cu.cuda(), max(lengths), rope=(cos.cuda(), sin.cuda()), **kw)
+    unfused = pe.packed_attention(rq.cuda(), rk.cuda(), v.cuda(), cu.cuda(), max(lengths), **kw)
+    torch.cuda.synchronize()
+    _assert_parity(out, ref, f"rope {lengths[:6]} H{heads}/{kv_heads} w{window} c{causal}")
+    assert (out != unfused).float().mean().item() < 0.01
+    assert pe.device_error_word() == 0
+
+
+def test_fused_rope_on_qkv_views():
+    """q and k as strided views of a fused qkv projection [T, 3, H, D] (forward.py:197-205), windowed
+    and global, with strided table views."""
+    pe = _b200()
+    lengths, heads = [40, 200, 7, 513], 12
+    total = sum(lengths)
+    gen = torch.Generator().manual_seed(9)
+    qkv = torch.randn(total, 3, heads, 64, generator=gen).to(torch.bfloat16)
+    cos, sin = rope_tables(lengths)
+    tables = torch.stack((cos, sin), 1)  # [T, 2, D]: each table a view with row stride 2*D
+    cu = torch.tensor([0] + lengths, dtype=torch.int32).cumsum(0, dtype=torch.int32)
+    for window in ((64, 64), (-1, -1)):
+        out = pe.packed_attention(qkv.cuda()[:, 0], qkv.cuda()[:, 1], qkv.cuda()[:, 2], cu.cuda(), max(lengths),
+                                  scale=0.125, window=window, rope=(tables.cuda()[:, 0], tables.cuda()[:, 1]))
+        rq, rk = oracle.rope_bshd(qkv[:, 0], cos, sin), oracle.rope_bshd(qkv[:, 1], cos, sin)
+        ref, _ = oracle.attention(rq, rk, qkv[:, 2].contiguous(), cu, scale=0.125, window=window)
+        _assert_parity(out, ref, f"rope qkv views {window}")
+    assert pe.device_error_word() == 0
+

@@ -90,6 +90,28 @@ def test_gate_stride_validation_without_touching_cuda():
     assert so.pe_b200_attn_fwd(ctypes.byref(_params(**base, gate=32, g_stride_token=768, g_stride_head=0)), None) == -3
 
 
+def test_rope_validation_without_touching_cuda():
+    """Rotary tables: both or neither, 16-byte aligned rows, head_dim 64 self-attention only; a bad
+    combination returns its status before any CUDA call."""
+    base = dict(q=16, k=16, v=16, out=16, cu_seqlens_q=16, cu_seqlens_k=16, workspace=256, workspace_bytes=1 << 20,
+                q_stride_token=768, q_stride_head=64, k_stride_token=768, k_stride_head=64, v_stride_token=768,
+                v_stride_head=64, o_stride_token=768, o_stride_head=64)
+    so = _lib.lib()
+
+    def status(**kw):
+        return so.pe_b200_attn_fwd(ctypes.byref(_params(**{**base, **kw})), None)
+
+    assert status(rope_cos=32, rope_stride_token=64) == -1                       # sin missing
+    assert status(rope_cos=40, rope_sin=32, rope_stride_token=64) == -3          # misaligned table
+    assert status(rope_cos=32, rope_sin=32, rope_stride_token=60) == -3          # rows narrower than D
+    assert status(rope_cos=32, rope_sin=32, rope_stride_token=68) == -3          # row stride not 16-byte
+    assert status(rope_cos=32, rope_sin=32, rope_stride_token=128, head_dim=128, q_stride_token=1536,
+                  q_stride_head=128, k_stride_token=1536, k_stride_head=128, v_stride_token=1536,
+                  v_stride_head=128, o_stride_token=1536, o_stride_head=128) == -8  # head_dim 128
+    assert status(rope_cos=32, rope_sin=32, rope_stride_token=64, cu_seqlens_k=48) == -8  # other key segments
+    assert status(rope_cos=32, rope_sin=32, rope_stride_token=64, total_k=999) == -8      # cross-attention
+
+
 def test_launch_entry_points_reject_null_workspace_without_touching_cuda():
     p = _params()
     so = _lib.lib()

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import golden_names, load_golden, packed_inputs
+from conftest import golden_names, load_golden, load_rope_golden, packed_inputs, rope_golden_names
 
 # fp32 restatement vs the reference's fp32 paths: both are fp32-exact to rounding.
 ATOL = 2e-5
@@ -95,3 +95,18 @@ def test_empty_batch_is_fine():
     q, k, v, cu = packed_inputs([0, 0], 2, 64)
     out, lse = oracle.attention(q, k, v, cu, scale=0.125)
     assert out.shape == (0, 2, 64) and lse.shape == (2, 0)
+
+
+@pytest.mark.parametrize("name", rope_golden_names())
+def test_rope_restatement_matches_reference(name):
+    """oracle.rope_bshd (fp32 rotate-half, rounded to bf16) against the reference's own CPU RoPE
+    (CPUAttention.rope_layout, fp32): equal up to the final bf16 rounding; and the reference's
+    attention over its rotated q/k is reproduced by the oracle over the restated rotation."""
+    g = load_rope_golden(name)
+    for x, ref in ((g["q"], g["rq"]), (g["k"], g["rk"])):
+        got = oracle.rope_bshd(x, g["cos"], g["sin"]).float()
+        assert ((got - ref).abs() <= ref.abs() * 2.0 ** -8 + 1e-6).all()
+    rq, rk = oracle.rope_bshd(g["q"], g["cos"], g["sin"]), oracle.rope_bshd(g["k"], g["cos"], g["sin"])
+    out, _ = oracle.attention(rq, rk, g["v"], g["cu_q"], scale=g["scale"], window=g["window"])
+    assert (out - g["out"]).abs().max().item() <= 2e-2
+
