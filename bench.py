@@ -392,6 +392,10 @@ def run_b200(args):
         except Exception as exc:  # noqa: BLE001
             record["config5_output_gate"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
         try:
+            record["config3_rope"] = rope_fusion(pe, wl)
+        except Exception as exc:  # noqa: BLE001
+            record["config3_rope"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
+        try:
             record["config4_full_forward"] = config4_forward(pe)
         except Exception as exc:  # noqa: BLE001
             record["config4_full_forward"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
@@ -585,6 +589,64 @@ def gate_fusion(pe, wl, iters=10):
         res[key] = round(statistics.median(vals), 4)
     res["speedup_vs_reference_gate"] = round(res["attention_then_reference_gate_ms"] / res["gated_call_ms"], 3)
     del q, k, v, gate, plan
+    return res
+
+
+def rope_fusion(pe, wl, iters=10):
+    """Config 3 layers with RoPE (ModernBERT's BSHD path, forward.py:197-205): q/k/v are views of
+    one packed qkv [T, 3*H*D] and the rotary tables are per token [T, 64]. One call
+    (packed_attention(..., rope=): this library's rope pass, then attention) against the
+    reference's apply_rope_bshd pass (_kernels/rope.py:302-345, CuteDSL) followed by the same
+    attention."""
+    w = wl.config3("mix")
+    lengths = w.lengths
+    q, k, v = wl.make_qkv(lengths, w.heads, w.kv_heads, w.head_dim, seed=1)
+    tq, h, d = q.shape
+    qkv = torch.stack((q, k, v), 1).reshape(tq, 3 * h * d)
+    del q, k, v
+    view = qkv.view(tq, 3, h, d)
+    cu = w.cu_seqlens().cuda()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    ref_rope = None
+    res = {}
+    if _reference_importable():
+        try:
+            from packed_encoders._kernels.rope import apply_rope_bshd as ref_rope
+        except Exception as exc:  # noqa: BLE001
+            res["reference_rope_kernel"] = f"unavailable: {type(exc).__name__}"
+    if ref_rope is None:
+        def ref_rope(x, heads, dim, cos, sin):
+            t = x.view(-1, 3, heads, dim)
+            rot = []
+            for part in (t[:, 0], t[:, 1]):
+                a, b = part.float().chunk(2, -1)
+                rot.append((part.float() * cos.float()[:, None] + torch.cat((-b, a), -1) * sin.float()[:, None])
+                           .to(x.dtype))
+            return rot[0], rot[1]
+        res["unfused_rope"] = "torch ops (reference rope kernel unavailable)"
+    for kind, (window, causal), theta in (("local", wl.LOCAL64, 10000.0), ("global", wl.GLOBAL, 160000.0)):
+        inv = 1.0 / theta ** (torch.arange(0, d, 2, dtype=torch.float32, device="cuda") / d)
+        pos = torch.cat([torch.arange(n, dtype=torch.float32, device="cuda") for n in lengths])
+        emb = torch.cat((pos[:, None] * inv, pos[:, None] * inv), -1)
+        cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+        kw = dict(scale=w.scale, window=window, causal=causal)  # both build their schedule per call
+
+        def fused():
+            pe.packed_attention(view[:, 0], view[:, 1], view[:, 2], cu, max(lengths), rope=(cos, sin), **kw)
+
+        def separate():
+            rq, rk = ref_rope(qkv, h, d, cos, sin)
+            pe.packed_attention(rq, rk, view[:, 2], cu, max(lengths), **kw)
+
+        times = {"rope_call_ms": [], "reference_rope_then_attention_ms": []}
+        for _ in range(3):
+            times["rope_call_ms"].append(_time_call(fused, iters, flush))
+            times["reference_rope_then_attention_ms"].append(_time_call(separate, iters, flush))
+        r = {key: round(statistics.median(val), 4) for key, val in times.items()}
+        r["speedup"] = round(r["reference_rope_then_attention_ms"] / r["rope_call_ms"], 3)
+        res[kind] = r
+        del cos, sin
+    del qkv, view
     return res
 
 

@@ -64,11 +64,12 @@ enum {
  *   on `stream` right after the attention kernel (or, with the environment variable
  *   PE_B200_GATE=fused, inside the attention epilogue); both give the same bits.
  * rope_cos, rope_sin [total_q, head_dim] bf16 (optional, both or neither; row stride
- *   rope_stride_token elements, D contiguous): q and k arrive un-rotated and the kernel applies
- *   the rotary embedding to each Q and K tile in shared memory before its MMA, with the
- *   reference's per-token tables and rotate-half rule (packed_encoders/_kernels/rope.py:5-6,
- *   140-200: y_lo = x_lo*cos - x_hi*sin, y_hi = x_hi*cos + x_lo*sin in fp32, rounded to bf16),
- *   replacing its separate apply_rope_bshd pass (packed_encoders/forward.py:199-205).
+ *   rope_stride_token elements, D contiguous): q and k arrive un-rotated (e.g. views of the fused
+ *   qkv projection); the call rotates them into the workspace (which then also holds
+ *   T*H*D + T*KV*D bf16, see pe_b200_attn_workspace_size) with the reference's per-token tables
+ *   and rotate-half rule (packed_encoders/_kernels/rope.py:5-6, 140-200: y_lo = x_lo*cos -
+ *   x_hi*sin, y_hi = x_hi*cos + x_lo*sin in fp32, rounded to bf16) and attends over the rotated
+ *   copies, in place of the reference's apply_rope_bshd pass (packed_encoders/forward.py:199-205).
  *   head_dim 64 and self-attention only (cu_seqlens_k == cu_seqlens_q, total_k == total_q);
  *   other calls with tables return PE_B200_ERR_UNSUPPORTED.
  *

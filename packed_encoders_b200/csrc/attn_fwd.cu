@@ -91,9 +91,6 @@ struct AttnParams {
   const __nv_bfloat16* gate;  // optional output gate [total_q, heads, D]
   long long g_tok;
   long long g_head;
-  const __nv_bfloat16* rope_cos;  // optional per-token rotary tables [total_q, D] (ROPE kernels)
-  const __nv_bfloat16* rope_sin;
-  long long rope_tok;
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -265,13 +262,10 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
 //   SPLIT softmax warps per 32-row TMEM lane quarter, each owning 1/SPLIT of the key columns and
 //        of O (more warps to hide latency at the same registers per row).
-//   ROPE the producer warp applies the rotary embedding to each Q and K tile in shared memory
-//        after its copy lands (per-token tables), and the MMA warp waits for that instead.
 template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1, int PASS_ = 0,
-          bool TMA_OUT_ = false, bool GATE_ = false, bool ROPE_ = false>
+          bool TMA_OUT_ = false, bool GATE_ = false>
 struct Cfg {
   static constexpr bool kGate = GATE_;  // output gate fused into the epilogue (calls with a gate)
-  static constexpr bool kRope = ROPE_;
   static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_,
                        SPLIT = SPLIT_;
   // S columns a softmax thread holds in registers at once (the row is re-read from TMEM for the
@@ -292,7 +286,7 @@ struct Cfg {
   static constexpr int kOffBar = kOffV + VST * kKVBytes;
   // barriers: k_full[ST] k_empty[ST] v_full[VST] v_empty[VST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS]
   //           o_full row_empty[QB]
-  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1 + (ROPE_ ? QB + ST : 0);
+  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr int kOffXchg = kOffTmemSlot + 16;  // row max [2][SPLIT][128] and sum [SPLIT][128], fp32
   static constexpr int kXchgBytes = SPLIT > 1 ? 3 * SPLIT * kTileM * 4 : 0;
@@ -318,7 +312,6 @@ struct Cfg {
   static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
   static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
-  static_assert(!ROPE_ || (D == 64 && SPLIT == 1 && !GATE_), "rotary tiles: head_dim 64, one warp per row");
   static_assert(BN % 64 == 0 && D % 64 == 0 && (BN / SPLIT) % kPass == 0 && kPass % 32 == 0, "tile shape");
   static_assert((BN / SPLIT) % 32 == 0 && (D / SPLIT) % 32 == 0 && SPLIT <= 2, "column split");
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
@@ -380,32 +373,38 @@ __global__ void __launch_bounds__(256) gate_pass_kernel(__nv_bfloat16* out, cons
   }
 }
 
-// Rotary embedding of `rows` 64-column bf16 rows of a 128B-swizzled tile in shared memory
-// (16-byte chunk c of row r at r*128 + (c ^ r % 8)*16), in place: row r is token tok0 + r and
-// uses that token's table rows; dims d and d+32 pair up (rotate-half):
-//   y[d] = x[d]*cos[d] - x[d+32]*sin[d],  y[d+32] = x[d+32]*cos[d+32] + x[d]*sin[d+32]
-// in fp32, rounded to bf16 (packed_encoders/_kernels/rope.py:5-6, 140-200). Rows past the
-// tensor (zero fill) stay as they are. One row per lane at a time.
-__device__ __forceinline__ void rope_rows(uint8_t* tile, int rows, int tok0, const AttnParams& p, int lane) {
-  for (int r = lane; r < rows; r += 32) {
-    const int tok = tok0 + r;
-    if (tok < 0 || tok >= p.total_q) continue;
-    uint8_t* row = tile + r * 128;
-    const int sw = r & 7;
-    uint4 x[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) x[c] = *reinterpret_cast<const uint4*>(row + ((c ^ sw) << 4));
-    const uint4* cs = reinterpret_cast<const uint4*>(p.rope_cos + (long long)tok * p.rope_tok);
-    const uint4* sn = reinterpret_cast<const uint4*>(p.rope_sin + (long long)tok * p.rope_tok);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint4 cl = __ldg(cs + c), ch = __ldg(cs + c + 4), sl = __ldg(sn + c), sh = __ldg(sn + c + 4);
-      const uint32_t lo[4] = {x[c].x, x[c].y, x[c].z, x[c].w}, hi[4] = {x[c + 4].x, x[c + 4].y, x[c + 4].z, x[c + 4].w};
+// Rotary embedding of q and k (head_dim 64) into contiguous [T, H, 64] / [T, KV, 64] buffers. Work
+// item i (grid-stride) = token i / (4 * (H + KV)) and, within it, t = i % (4 * (H + KV)): the 16
+// elements of dims {8c..8c+7} and {8c+32..8c+39} (c = t % 4) of one head of q (t < 4H) or k.
+// A token's table row is shared by its heads (L1). Per element pair, in fp32 rounded to bf16
+// (packed_encoders/_kernels/rope.py:5-6, 140-200; the reference CPU path cpu/attention.py:298-301):
+//   y[d] = x[d]*cos[d] - x[d+32]*sin[d],  y[d+32] = x[d+32]*cos[d+32] + x[d]*sin[d+32].
+__global__ void __launch_bounds__(256) rope_pass_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k,
+                                                        long long q_tok, long long q_head, long long k_tok,
+                                                        long long k_head, const __nv_bfloat16* cos_t,
+                                                        const __nv_bfloat16* sin_t, long long t_tok, int total,
+                                                        int heads, int kv_heads, __nv_bfloat16* q_out,
+                                                        __nv_bfloat16* k_out) {
+  const int per_tok = 4 * (heads + kv_heads);
+  const long long n = (long long)total * per_tok;
+  auto e0 = [](uint32_t v) { return __uint_as_float(v << 16); };
+  auto e1 = [](uint32_t v) { return __uint_as_float(v & 0xffff0000u); };
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    {
+      const int tok = (int)(i / per_tok), t = (int)(i - (long long)tok * per_tok);
+      const int c = t & 3, hh = t >> 2;
+      const bool is_q = hh < heads;
+      const int h = is_q ? hh : hh - heads;
+      const __nv_bfloat16* src = is_q ? q + (long long)tok * q_tok + (long long)h * q_head
+                                      : k + (long long)tok * k_tok + (long long)h * k_head;
+      __nv_bfloat16* dst = is_q ? q_out + ((long long)tok * heads + h) * 64 : k_out + ((long long)tok * kv_heads + h) * 64;
+      const uint4* c4 = reinterpret_cast<const uint4*>(cos_t + (long long)tok * t_tok);
+      const uint4* s4 = reinterpret_cast<const uint4*>(sin_t + (long long)tok * t_tok);
+      const uint4 xl = __ldg(reinterpret_cast<const uint4*>(src) + c), xh = __ldg(reinterpret_cast<const uint4*>(src) + c + 4);
+      const uint4 cl = __ldg(c4 + c), ch = __ldg(c4 + c + 4), sl = __ldg(s4 + c), sh = __ldg(s4 + c + 4);
+      const uint32_t lo[4] = {xl.x, xl.y, xl.z, xl.w}, hi[4] = {xh.x, xh.y, xh.z, xh.w};
       const uint32_t cl4[4] = {cl.x, cl.y, cl.z, cl.w}, ch4[4] = {ch.x, ch.y, ch.z, ch.w};
       const uint32_t sl4[4] = {sl.x, sl.y, sl.z, sl.w}, sh4[4] = {sh.x, sh.y, sh.z, sh.w};
-      // bf16 pair word: element 0 in the low half, element 1 in the high half
-      auto e0 = [](uint32_t v) { return __uint_as_float(v << 16); };
-      auto e1 = [](uint32_t v) { return __uint_as_float(v & 0xffff0000u); };
       uint32_t ylo[4], yhi[4];
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
@@ -413,11 +412,9 @@ __device__ __forceinline__ void rope_rows(uint8_t* tile, int rows, int tok0, con
         ylo[w] = pack_bf16x2(a0 * e0(cl4[w]) - b0 * e0(sl4[w]), a1 * e1(cl4[w]) - b1 * e1(sl4[w]));
         yhi[w] = pack_bf16x2(b0 * e0(ch4[w]) + a0 * e0(sh4[w]), b1 * e1(ch4[w]) + a1 * e1(sh4[w]));
       }
-      x[c] = make_uint4(ylo[0], ylo[1], ylo[2], ylo[3]);
-      x[c + 4] = make_uint4(yhi[0], yhi[1], yhi[2], yhi[3]);
+      reinterpret_cast<uint4*>(dst)[c] = make_uint4(ylo[0], ylo[1], ylo[2], ylo[3]);
+      reinterpret_cast<uint4*>(dst)[c + 4] = make_uint4(yhi[0], yhi[1], yhi[2], yhi[3]);
     }
-#pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) = x[c];
   }
 }
 
@@ -596,8 +593,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   uint64_t* p_full = s_full + C::NS;
   uint64_t* o_full = p_full + C::NS;  // the last P.V of each unit (epilogue)
   uint64_t* row_empty = o_full + 1;    // [QB] the softmax warps took the unit's row slot
-  uint64_t* q_ready = row_empty + C::QB;  // [QB] (ROPE) the producer rotated the unit's Q tile
-  uint64_t* k_ready = q_ready + C::QB;    // [ST] (ROPE) the producer rotated the K tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -622,10 +617,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     }
     mbar_init(o_full, 1);
     for (int i = 0; i < C::QB; ++i) mbar_init(&row_empty[i], 4 * C::SPLIT);
-    if constexpr (C::kRope) {
-      for (int i = 0; i < C::QB; ++i) mbar_init(&q_ready[i], 1);
-      for (int i = 0; i < C::ST; ++i) mbar_init(&k_ready[i], 1);
-    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -665,48 +656,9 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       int lu = 0;
       int v_row = 0, v_head = 0;
       bool v_pending = false;
-      // ROPE: rotations of landed Q / K tiles, done in issue order two copies behind (by then the
-      // copy has usually landed) and whenever the producer would otherwise wait on a consumer.
-      struct Rot {
-        uint8_t* tile;
-        uint64_t* full;
-        uint64_t* ready;
-        int parity, tok0, rows;
-      };
-      Rot rots[8];
-      int rot_head = 0, rot_n = 0;
-      auto rot_flush = [&](int keep) {
-        if constexpr (C::kRope) {
-          while (rot_n > keep) {
-            const Rot r = rots[rot_head];
-            rot_head = (rot_head + 1) & 7;
-            --rot_n;
-            mbar_wait(r.full, r.parity, p.err);
-            rope_rows(r.tile, r.rows, r.tok0, p, lane);
-            fence_proxy_async_smem();  // these generic-proxy stores before the MMA's reads
-            __syncwarp();
-            if (lane == 0) mbar_arrive(r.ready);
-          }
-        }
-      };
-      auto rot_push = [&](uint8_t* tile, uint64_t* full, uint64_t* ready, int parity, int tok0, int rows) {
-        if constexpr (C::kRope) {
-          rots[(rot_head + rot_n) & 7] = Rot{tile, full, ready, parity, tok0, rows};
-          ++rot_n;
-          rot_flush(2);
-        }
-      };
-      // A wait on a consumer that would block first does the pending rotations (the consumers
-      // may need them to make progress).
-      auto wait_consumer = [&](uint64_t* bar, int parity) {
-        if constexpr (C::kRope) {
-          if (rot_n > 0 && !mbar_test_wait(bar, (uint32_t)parity)) rot_flush(0);
-        }
-        mbar_wait(bar, parity, p.err);
-      };
       auto issue_v = [&](long long j, int row, int kvh) {
         const int st = (int)(j % C::VST);
-        if (j >= C::VST) wait_consumer(&v_empty[st], (int)((j / C::VST) - 1) & 1);
+        if (j >= C::VST) mbar_wait(&v_empty[st], (int)((j / C::VST) - 1) & 1, p.err);
         uint8_t* vs = smem + C::kOffV + st * C::kKVBytes;
         mbar_arrive_expect_tx_w(&v_full[st], C::kKVBytes);
         if constexpr (C::kPanels > 1) {
@@ -719,7 +671,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
-        if (lu >= C::QB) wait_consumer(&q_empty[qb], ((lu / C::QB) - 1) & 1);
+        if (lu >= C::QB) mbar_wait(&q_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
         // The Q copy goes first (its bytes are expected before the arrival), then the row slot;
         // the producer's arrival on q_full, after the slot stores, publishes both.
         uint8_t* qs = smem + C::kOffQ + qb * C::kQBytes;
@@ -730,14 +682,13 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         } else {
           load_q(qs, 0, ui.head, ui.q_row0, &q_full[qb]);
         }
-        if (lu >= C::QB) wait_consumer(&row_empty[qb], ((lu / C::QB) - 1) & 1);
+        if (lu >= C::QB) mbar_wait(&row_empty[qb], ((lu / C::QB) - 1) & 1, p.err);
         write_row_slot<C>(p, ui, smem + C::kOffRows + qb * C::kRowSlotBytes, lane);
         __syncwarp();  // the slot stores are ordered before the q_full arrival
         if (lane == 0) mbar_arrive(&q_full[qb]);
-        rot_push(qs, &q_full[qb], &q_ready[qb], (lu / C::QB) & 1, ui.q_row0, kTileM);
         for (int t = 0; t < ui.n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
-          if (i >= C::ST) wait_consumer(&k_empty[st], (int)((i / C::ST) - 1) & 1);
+          if (i >= C::ST) mbar_wait(&k_empty[st], (int)((i / C::ST) - 1) & 1, p.err);
           const int row = ui.kv_lo + t * C::BN;
           uint8_t* ks = smem + C::kOffK + st * C::kKVBytes;
           mbar_arrive_expect_tx_w(&k_full[st], C::kKVBytes);
@@ -746,7 +697,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           } else {
             load_kv(ks, &tm_k, 0, ui.kv_head, row, &k_full[st]);
           }
-          rot_push(ks, &k_full[st], &k_ready[st], (int)(i / C::ST) & 1, row, C::BN);
           if (v_pending) issue_v(i - 1, v_row, v_head);
           v_pending = true;
           v_row = row;
@@ -755,7 +705,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         ++lu;
       }
       if (v_pending) issue_v(i - 1, v_row, v_head);
-      rot_flush(0);
       {  // end marker for the softmax warps: a slot with n_kv = -1, published through q_full
         const int qb = lu % C::QB;
         if (lu >= C::QB) {
@@ -835,7 +784,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         // The previous unit's last P.Vs go before this unit's first QK: the softmax warps run
         // that unit's epilogue before they can use the new S, so its O is what they wait for.
         while (npend > 0) flush_one();
-        mbar_wait(C::kRope ? &q_ready[qb] : &q_full[qb], (lu / C::QB) & 1, p.err);
+        mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
         tc_fence_after();
         const uint32_t q_addr = smem_base + C::kOffQ + qb * C::kQBytes;
         for (int t = 0; t < ui.n_kv; ++t, ++i) {
@@ -844,7 +793,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           // With one S buffer the previous P must be consumed first (issue order = execution order).
           if (C::NS == 1)
             while (npend > 0) flush_one();
-          mbar_wait(C::kRope ? &k_ready[st] : &k_full[st], (int)(i / C::ST) & 1, p.err);
+          mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
           if constexpr (C::kGroupMma) {
@@ -1442,7 +1391,6 @@ static int env_int(const char* name, int fallback) {
 // 8.25): in the fused form the two MUFU operations per element of the sigmoid run on the softmax
 // warps between one unit and the next, while the pass streams at memory speed.
 static bool gate_as_own_pass(const PeB200AttnParams* p) {
-  if (p->rope_cos) return true;  // the rotary kernels carry no gate epilogue
   const char* e = getenv("PE_B200_GATE");
   return !(e && strcmp(e, "fused") == 0);
 }
@@ -1464,7 +1412,16 @@ static long long item_capacity(const PeB200AttnParams* p) {
   return (long long)p->n_seq + (long long)p->total_q / kTileM + 2;
 }
 
+// Rotary calls keep their rotated q and k in the workspace, after the schedule (256-byte aligned).
+static size_t rope_q_offset(const PeB200AttnParams* p) {
+  return ((size_t)kHeaderBytes + sizeof(WorkItem) * (size_t)item_capacity(p) + 255) & ~(size_t)255;
+}
+static size_t rope_k_offset(const PeB200AttnParams* p) {
+  return (rope_q_offset(p) + (size_t)p->total_q * p->heads * p->head_dim * 2 + 255) & ~(size_t)255;
+}
+
 static size_t workspace_bytes_for(const PeB200AttnParams* p) {
+  if (p->rope_cos) return rope_k_offset(p) + (size_t)p->total_k * p->kv_heads * p->head_dim * 2;
   return (size_t)kHeaderBytes + sizeof(WorkItem) * (size_t)item_capacity(p);
 }
 
@@ -1545,9 +1502,6 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   ap.gate = static_cast<const __nv_bfloat16*>(p->gate);
   ap.g_tok = p->g_stride_token;
   ap.g_head = p->g_stride_head;
-  ap.rope_cos = static_cast<const __nv_bfloat16*>(p->rope_cos);
-  ap.rope_sin = static_cast<const __nv_bfloat16*>(p->rope_sin);
-  ap.rope_tok = p->rope_stride_token;
   const long long units = item_capacity(p) * p->heads;
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
@@ -1669,6 +1623,28 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   const DeviceInfo& info = device_info(dev);
   if (info.supported != 1) return PE_B200_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->rope_cos) {  // rotary tables (validated: head_dim 64, self-attention): rotate, then attend
+    uint8_t* ws = static_cast<uint8_t*>(p->workspace);
+    __nv_bfloat16* q_rot = reinterpret_cast<__nv_bfloat16*>(ws + rope_q_offset(p));
+    __nv_bfloat16* k_rot = reinterpret_cast<__nv_bfloat16*>(ws + rope_k_offset(p));
+    const int grid = (int)(p->total_q < info.sms * 8 ? p->total_q : info.sms * 8);
+    rope_pass_kernel<<<grid, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(p->q), static_cast<const __nv_bfloat16*>(p->k), p->q_stride_token,
+        p->q_stride_head, p->k_stride_token, p->k_stride_head, static_cast<const __nv_bfloat16*>(p->rope_cos),
+        static_cast<const __nv_bfloat16*>(p->rope_sin), p->rope_stride_token, p->total_q, p->heads, p->kv_heads, q_rot,
+        k_rot);
+    st = launch_status("rope_pass_kernel launch");
+    if (st != PE_B200_OK) return st;
+    PeB200AttnParams r = *p;
+    r.rope_cos = r.rope_sin = nullptr;
+    r.q = q_rot;
+    r.k = k_rot;
+    r.q_stride_token = (int64_t)p->heads * 64;
+    r.q_stride_head = 64;
+    r.k_stride_token = (int64_t)p->kv_heads * 64;
+    r.k_stride_head = 64;
+    return pe_b200_attn_run(&r, stream);
+  }
   if (p->gate && gate_as_own_pass(p)) {
     PeB200AttnParams ungated = *p;
     ungated.gate = nullptr;
@@ -1692,11 +1668,6 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
       case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 1, 0, false, true>>(p, s, info.sms);
       default: return PE_B200_ERR_UNSUPPORTED;
     }
-  }
-  if (p->rope_cos) {  // rotary tables (validated: head_dim 64, self-attention)
-    if ((p->window_left >= 0 || p->window_right >= 0) && !p->causal)
-      return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 1, 0, true, false, true>>(p, s, info.sms);
-    return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1, 0, false, false, true>>(p, s, info.sms);
   }
   switch (p->head_dim) {
     case 64:

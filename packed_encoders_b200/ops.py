@@ -177,10 +177,10 @@ def packed_attention(
     ``out = bf16(o * bf16(sigmoid(gate)))`` with ``o`` the bf16 attention output, the roundings
     of the reference's ``sigmoid_gate`` (_kernels/hybrid.py:196-205); the LSE is not gated.
     ``rope`` ``(cos, sin)``, each ``[Tq, D]`` bf16 per-token tables (D contiguous, one row
-    stride): q and k are given un-rotated (e.g. views of the fused qkv projection) and the kernel
-    rotates each Q and K tile in shared memory, the reference's rotate-half rule of
-    ``apply_rope_bshd`` (_kernels/rope.py:140-200) fused into the attention instead of a pass of
-    its own (forward.py:199-205). head_dim 64, self-attention (no ``cu_seqlens_k``) only.
+    stride): q and k are given un-rotated (e.g. views of the fused qkv projection); the call
+    rotates them (the reference's rotate-half rule of ``apply_rope_bshd``, _kernels/rope.py:140-200,
+    used at forward.py:199-205) into its workspace with this library's rope pass, then attends.
+    head_dim 64, self-attention (no ``cu_seqlens_k``), no ``plan``.
     """
     _check_qkv(q, k, v)
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
@@ -210,7 +210,9 @@ def packed_attention(
                 or cos.stride(0) != sin.stride(0) or cos.device != q.device or sin.device != q.device):
             raise UnsupportedTargetError("rope tables must be bf16 [Tq, D] with a contiguous D and one row stride")
         if dim != 64 or cu_seqlens_k is not None or tk != tq:
-            raise UnsupportedTargetError("fused rope: head_dim 64 self-attention only")
+            raise UnsupportedTargetError("rope: head_dim 64 self-attention only")
+        if plan is not None:
+            raise UnsupportedTargetError("rope calls keep the rotated q/k in their own workspace: omit plan")
     if gate is not None and (gate.shape != q.shape or gate.dtype != torch.bfloat16 or gate.stride(2) != 1
                              or gate.device != q.device):
         raise UnsupportedTargetError("gate must be bf16 with q's shape and a contiguous head_dim")

@@ -92,8 +92,9 @@ def test_gate_stride_validation_without_touching_cuda():
 
 def test_rope_validation_without_touching_cuda():
     """Rotary tables: both or neither, 16-byte aligned rows, head_dim 64 self-attention only; a bad
-    combination returns its status before any CUDA call."""
-    base = dict(q=16, k=16, v=16, out=16, cu_seqlens_q=16, cu_seqlens_k=16, workspace=256, workspace_bytes=1 << 20,
+    combination returns its status before any CUDA call. (Rotary calls need a workspace that also
+    holds the rotated q and k.)"""
+    base = dict(q=16, k=16, v=16, out=16, cu_seqlens_q=16, cu_seqlens_k=16, workspace=256, workspace_bytes=1 << 40,
                 q_stride_token=768, q_stride_head=64, k_stride_token=768, k_stride_head=64, v_stride_token=768,
                 v_stride_head=64, o_stride_token=768, o_stride_head=64)
     so = _lib.lib()
@@ -110,6 +111,14 @@ def test_rope_validation_without_touching_cuda():
                   v_stride_head=128, o_stride_token=1536, o_stride_head=128) == -8  # head_dim 128
     assert status(rope_cos=32, rope_sin=32, rope_stride_token=64, cu_seqlens_k=48) == -8  # other key segments
     assert status(rope_cos=32, rope_sin=32, rope_stride_token=64, total_k=999) == -8      # cross-attention
+    need = ctypes.c_size_t(0)
+    plain = _params(**base)
+    rope = _params(**{**base, "rope_cos": 32, "rope_sin": 32, "rope_stride_token": 64})
+    assert so.pe_b200_attn_workspace_size(ctypes.byref(plain), ctypes.byref(need)) == 0
+    plain_bytes = need.value
+    assert so.pe_b200_attn_workspace_size(ctypes.byref(rope), ctypes.byref(need)) == 0
+    assert need.value >= plain_bytes + 2 * 1000 * 12 * 64 * 2  # + rotated q and k
+    assert status(rope_cos=32, rope_sin=32, rope_stride_token=64, workspace_bytes=plain_bytes) == -5
 
 
 def test_launch_entry_points_reject_null_workspace_without_touching_cuda():
