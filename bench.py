@@ -739,8 +739,10 @@ def run_reference(args):
 
 
 def run_case(args):
-    """Profiling helper: ``--case NAME --iters N [--seqs S]`` launches one configuration N times
-    (no timing output), e.g. for an ncu capture of a small case of the same kernel."""
+    """Profiling helper: ``--case NAME --iters N [--seqs S] [--rope] [--gate]`` launches one
+    configuration N times (no timing output), e.g. for an ncu capture of a small case of the same
+    kernel. ``--rope``: q/k/v are views of one packed qkv and the call applies RoPE (head_dim 64);
+    ``--gate``: the call applies the output gate."""
     import packed_encoders_b200 as pe
     from packed_encoders_b200 import workloads as wl
 
@@ -754,9 +756,19 @@ def run_case(args):
     cu[1:] = torch.tensor(lengths).cumsum(0)
     cu = cu.cuda()
     (window, causal), = set(w.layers)
-    out = torch.empty_like(q)
+    extra = {}
+    if args.rope:
+        qkv = torch.stack((q, k, v), 1)
+        q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+        inv = 1.0 / 10000.0 ** (torch.arange(0, 64, 2, dtype=torch.float32, device="cuda") / 64)
+        pos = torch.cat([torch.arange(n, dtype=torch.float32, device="cuda") for n in lengths])
+        emb = torch.cat((pos[:, None] * inv, pos[:, None] * inv), -1)
+        extra["rope"] = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16))
+    if args.gate:
+        extra["gate"] = torch.randn(q.shape, device="cuda").to(torch.bfloat16)
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     for _ in range(args.iters):
-        pe.packed_attention(q, k, v, cu, max(lengths), scale=w.scale, window=window, causal=causal, out=out)
+        pe.packed_attention(q, k, v, cu, max(lengths), scale=w.scale, window=window, causal=causal, out=out, **extra)
     torch.cuda.synchronize()
     print(json.dumps({"case": args.case, "tokens": sum(lengths), "seqs": len(lengths), "iters": args.iters,
                       "device_error_word": pe.device_error_word()}))
@@ -767,6 +779,8 @@ def main():
     ap.add_argument("--case", default=None, help="profiling helper: run one configuration --iters times")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--seqs", type=int, default=0, help="with --case: use only the first SEQS sequences")
+    ap.add_argument("--rope", action="store_true", help="with --case: q/k/v views of one qkv, RoPE in the call")
+    ap.add_argument("--gate", action="store_true", help="with --case: output gate in the call")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
