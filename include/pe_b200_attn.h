@@ -168,6 +168,21 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream);
 int pe_b200_attn_fwd_noalloc(const PeB200AttnParams* p, void* stream);
 
 /*
+ * Rotary embedding of q and k into contiguous copies, the reference's BSHD RoPE pass
+ * (packed_encoders/_kernels/rope.py:302-345, apply_rope_bshd; rotate-half in fp32 rounded to
+ * bf16, rope.py:5-6): q [total, heads, 64] and k [total, kv_heads, 64] bf16 with any 16-byte
+ * token / head strides (D contiguous; e.g. views of the fused qkv projection); cos / sin bf16
+ * tables with 64-element rows, row stride table_stride_token; token t uses row t % table_rows
+ * (table_rows = total for per-token gathered tables, S for one [S, 64] table over a [B, S]
+ * batch). Writes q_out [total, heads, 64] and k_out [total, kv_heads, 64] contiguous, enqueued
+ * on `stream`. head_dim must be 64 (PE_B200_ERR_UNSUPPORTED otherwise).
+ */
+int pe_b200_rope_qk(const void* q, const void* k, int64_t q_stride_token, int64_t q_stride_head,
+                    int64_t k_stride_token, int64_t k_stride_head, const void* cos_table, const void* sin_table,
+                    int64_t table_stride_token, int32_t table_rows, int32_t total, int32_t heads, int32_t kv_heads,
+                    int32_t head_dim, void* q_out, void* k_out, void* stream);
+
+/*
  * Debug / layout probes (one CTA, no schedule): QK^T of one 128-row query tile against one
  * key tile into fp32 s_out [128, block_n]; and P.V with fp32 p_in [128, block_n] rounded to
  * bf16 through TMEM into fp32 o_out [128, head_dim]. Rows/keys past the given counts are

@@ -5,6 +5,7 @@ Public entry points mirror the reference's attention hooks; see ``ops`` for the 
 
 from packed_encoders_b200.errors import PackedEncodersError, UnsupportedTargetError, ValidationError
 from packed_encoders_b200.ops import (
+    apply_rope_bshd,
     attention_bshd,
     device_error_word,
     flash_attention_varlen,
@@ -15,6 +16,6 @@ from packed_encoders_b200.ops import (
 
 __all__ = [
     "PackedEncodersError", "UnsupportedTargetError", "ValidationError",
-    "attention_bshd", "device_error_word", "flash_attention_varlen", "packed_attention",
+    "apply_rope_bshd", "attention_bshd", "device_error_word", "flash_attention_varlen", "packed_attention",
     "packed_short_attention", "packed_short_attention_supported",
 ]

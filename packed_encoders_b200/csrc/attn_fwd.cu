@@ -382,8 +382,8 @@ __global__ void __launch_bounds__(256) gate_pass_kernel(__nv_bfloat16* out, cons
 __global__ void __launch_bounds__(256) rope_pass_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k,
                                                         long long q_tok, long long q_head, long long k_tok,
                                                         long long k_head, const __nv_bfloat16* cos_t,
-                                                        const __nv_bfloat16* sin_t, long long t_tok, int total,
-                                                        int heads, int kv_heads, __nv_bfloat16* q_out,
+                                                        const __nv_bfloat16* sin_t, long long t_tok, int t_rows,
+                                                        int total, int heads, int kv_heads, __nv_bfloat16* q_out,
                                                         __nv_bfloat16* k_out) {
   const int per_tok = 4 * (heads + kv_heads);
   const long long n = (long long)total * per_tok;
@@ -398,8 +398,9 @@ __global__ void __launch_bounds__(256) rope_pass_kernel(const __nv_bfloat16* q, 
       const __nv_bfloat16* src = is_q ? q + (long long)tok * q_tok + (long long)h * q_head
                                       : k + (long long)tok * k_tok + (long long)h * k_head;
       __nv_bfloat16* dst = is_q ? q_out + ((long long)tok * heads + h) * 64 : k_out + ((long long)tok * kv_heads + h) * 64;
-      const uint4* c4 = reinterpret_cast<const uint4*>(cos_t + (long long)tok * t_tok);
-      const uint4* s4 = reinterpret_cast<const uint4*>(sin_t + (long long)tok * t_tok);
+      const int trow = tok < t_rows ? tok : tok % t_rows;  // dense [S, 64] tables over a [B, S] batch
+      const uint4* c4 = reinterpret_cast<const uint4*>(cos_t + (long long)trow * t_tok);
+      const uint4* s4 = reinterpret_cast<const uint4*>(sin_t + (long long)trow * t_tok);
       const uint4 xl = __ldg(reinterpret_cast<const uint4*>(src) + c), xh = __ldg(reinterpret_cast<const uint4*>(src) + c + 4);
       const uint4 cl = __ldg(c4 + c), ch = __ldg(c4 + c + 4), sl = __ldg(s4 + c), sh = __ldg(s4 + c + 4);
       const uint32_t lo[4] = {xl.x, xl.y, xl.z, xl.w}, hi[4] = {xh.x, xh.y, xh.z, xh.w};
@@ -1631,8 +1632,8 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
     rope_pass_kernel<<<grid, 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(p->q), static_cast<const __nv_bfloat16*>(p->k), p->q_stride_token,
         p->q_stride_head, p->k_stride_token, p->k_stride_head, static_cast<const __nv_bfloat16*>(p->rope_cos),
-        static_cast<const __nv_bfloat16*>(p->rope_sin), p->rope_stride_token, p->total_q, p->heads, p->kv_heads, q_rot,
-        k_rot);
+        static_cast<const __nv_bfloat16*>(p->rope_sin), p->rope_stride_token, p->total_q, p->total_q, p->heads,
+        p->kv_heads, q_rot, k_rot);
     st = launch_status("rope_pass_kernel launch");
     if (st != PE_B200_OK) return st;
     PeB200AttnParams r = *p;
@@ -1697,6 +1698,37 @@ int pe_b200_attn_fwd(const PeB200AttnParams* p, void* stream) {
   st = pe_b200_build_schedule(p, stream);
   if (st != PE_B200_OK) return st;
   return pe_b200_attn_run(p, stream);
+}
+
+int pe_b200_rope_qk(const void* q, const void* k, int64_t q_stride_token, int64_t q_stride_head,
+                    int64_t k_stride_token, int64_t k_stride_head, const void* cos_table, const void* sin_table,
+                    int64_t table_stride_token, int32_t table_rows, int32_t total, int32_t heads, int32_t kv_heads,
+                    int32_t head_dim, void* q_out, void* k_out, void* stream) {
+  if (total < 0 || heads < 1 || kv_heads < 1 || table_rows < 1) return PE_B200_ERR_SHAPE;
+  if (head_dim != 64) return PE_B200_ERR_UNSUPPORTED;
+  if (total == 0) return PE_B200_OK;
+  if (!q || !k || !cos_table || !sin_table || !q_out || !k_out) return PE_B200_ERR_NULL;
+  auto aligned16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!aligned16(q) || !aligned16(k) || !aligned16(cos_table) || !aligned16(sin_table) || !aligned16(q_out) ||
+      !aligned16(k_out))
+    return PE_B200_ERR_STRIDE;
+  const int64_t strides[5] = {q_stride_token, q_stride_head, k_stride_token, k_stride_head, table_stride_token};
+  for (int64_t s : strides)
+    if (s <= 0 || (s * 2) % 16 != 0) return PE_B200_ERR_STRIDE;
+  if (table_stride_token < 64) return PE_B200_ERR_STRIDE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PE_B200_ERR_CUDA;
+  const DeviceInfo& info = device_info(dev);
+  if (info.supported != 1) return PE_B200_ERR_DEVICE;
+  const long long items = (long long)total * 4 * (heads + kv_heads);
+  const long long blocks = (items + 255) / 256;
+  const int grid = (int)(blocks < info.sms * 8 ? blocks : info.sms * 8);
+  rope_pass_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), q_stride_token, q_stride_head,
+      k_stride_token, k_stride_head, static_cast<const __nv_bfloat16*>(cos_table),
+      static_cast<const __nv_bfloat16*>(sin_table), table_stride_token, table_rows, total, heads, kv_heads,
+      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out));
+  return launch_status("rope_pass_kernel launch");
 }
 
 int pe_b200_debug_qk(const void* q, const void* k, int64_t q_stride_token, int64_t k_stride_token, int rows_q,

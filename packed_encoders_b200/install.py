@@ -66,13 +66,26 @@ def b200_attention_bshd_piece():
     return Piece("attention-bshd-b200", BSHD, _execute_bshd, _reference_bshd, _check_bshd)
 
 
+def _execute_rope_qkv(qkv, h, d, cos, sin):
+    return b200_ops.apply_rope_bshd(qkv, h, d, cos, sin)
+
+
+def b200_rope_qkv_piece():
+    """The QKV-BSHD RoPE piece (contract pieces/rope.py:97-99) executed by this library's rope
+    pass, with the reference's own oracle and argument checks (pieces/rope.py:73-80)."""
+    from packed_encoders.pieces.rope import QKV_BSHD, RoPEPiece, check_qkv, reference_qkv
+
+    return RoPEPiece("split-half-rope-qkv-bshd-b200", QKV_BSHD, _execute_rope_qkv, reference_qkv, check_qkv)
+
+
 def b200_pieces(base=None):
-    """ModernBERT pieces with the attention slot replaced (docs/architectures.md:139-149)."""
+    """ModernBERT pieces with the BSHD attention and QKV RoPE slots replaced
+    (docs/architectures.md:139-149)."""
     if base is None:
         from packed_encoders.arch.modernbert_pieces import default_pieces
 
         base = default_pieces()
-    return dataclasses.replace(base, attention_bshd=b200_attention_bshd_piece())
+    return dataclasses.replace(base, attention_bshd=b200_attention_bshd_piece(), rope_qkv=b200_rope_qkv_piece())
 
 
 # --------------------------------------------------------------------------- runtime candidate
@@ -196,4 +209,4 @@ def install() -> None:
     _INSTALLED["done"] = True
 
 
-__all__ = ["BACKEND", "b200_attention_bshd_piece", "b200_candidate", "b200_pieces", "install"]
+__all__ = ["BACKEND", "b200_attention_bshd_piece", "b200_candidate", "b200_pieces", "b200_rope_qkv_piece", "install"]

@@ -336,3 +336,38 @@ def debug_pv(p: Tensor, v: Tensor) -> Tensor:
     _lib.check(_lib.lib().pe_b200_debug_pv(p.data_ptr(), v.data_ptr(), v.stride(0), v.shape[0], v.shape[1],
                                            o.data_ptr(), stream.cuda_stream), "debug_pv")
     return o
+
+
+def apply_rope_bshd(qkv: Tensor, h: int, d: int, cos: Tensor, sin: Tensor) -> tuple[Tensor, Tensor]:
+    """RoPE'd q, k from the packed qkv ``[..., 3*H*D]`` (the fused Wqkv output), contiguous
+    ``[..., H, D]``: the reference's ``apply_rope_bshd`` (_kernels/rope.py:302-345, same arguments
+    and rotate-half rule, fp32 rounded to bf16) on this library's rope pass. ``cos``/``sin`` are
+    ``[S, D]`` (or ``[1, S, D]``) position tables of a dense ``[B, S]`` batch (row ``t % S``) or the
+    per-token gathered ``[total, D]`` tables of a packed batch. head_dim 64."""
+    if qkv.dtype != torch.bfloat16 or not qkv.is_cuda or qkv.shape[-1] != 3 * h * d or qkv.stride(-1) != 1:
+        raise UnsupportedTargetError("rope: qkv must be CUDA bf16 [..., 3*H*D] with a contiguous last dim")
+    if d != 64:
+        raise UnsupportedTargetError("rope: head_dim 64 only")
+    if cos.ndim == 3:
+        cos, sin = cos[0], sin[0]
+    if (cos.shape != sin.shape or cos.ndim != 2 or cos.shape[1] != d or cos.dtype != torch.bfloat16
+            or sin.dtype != torch.bfloat16 or cos.stride(1) != 1 or sin.stride(1) != 1 or cos.stride(0) != sin.stride(0)
+            or cos.device != qkv.device or sin.device != qkv.device):
+        raise UnsupportedTargetError("rope: cos/sin must be bf16 [S, D] tables on qkv's device with one row stride")
+    rows = qkv.reshape(-1, 3 * h * d)
+    n = rows.shape[0]
+    view = rows.view(n, 3, h, d)
+    q_out = torch.empty(n, h, d, dtype=qkv.dtype, device=qkv.device)
+    k_out = torch.empty(n, h, d, dtype=qkv.dtype, device=qkv.device)
+    if n:
+        with torch.cuda.device(qkv.device):
+            stream = torch.cuda.current_stream(qkv.device)
+            q, k = view[:, 0], view[:, 1]
+            _lib.check(_lib.lib().pe_b200_rope_qk(
+                _ptr(q), _ptr(k), q.stride(0), q.stride(1), k.stride(0), k.stride(1), _ptr(cos), _ptr(sin),
+                cos.stride(0), cos.shape[0], n, h, h, d, _ptr(q_out), _ptr(k_out), ctypes.c_void_p(stream.cuda_stream)),
+                "pe_b200_rope_qk")
+        _count(1)
+    shape = tuple(qkv.shape[:-1]) + (h, d)
+    return q_out.view(shape), k_out.view(shape)
+

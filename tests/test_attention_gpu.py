@@ -356,3 +356,32 @@ def test_fused_rope_on_qkv_views():
         _assert_parity(out, ref, f"rope qkv views {window}")
     assert pe.device_error_word() == 0
 
+
+
+@pytest.mark.parametrize("dense", [False, True])
+def test_apply_rope_bshd_matches_oracle(dense):
+    """The standalone RoPE pass (the reference's apply_rope_bshd signature, _kernels/rope.py:302-345)
+    against the oracle's rotate-half restatement: per-token gathered tables of a packed batch, and
+    one dense [S, D] table over a [B, S] batch (row t % S)."""
+    pe = _b200()
+    heads, d = 12, 64
+    gen = torch.Generator().manual_seed(13)
+    if dense:
+        b, s = 3, 200
+        qkv = torch.randn(b, s, 3 * heads * d, generator=gen).to(torch.bfloat16)
+        cos, sin = rope_tables([s], theta=160000.0)
+        rows_cos, rows_sin = cos.repeat(b, 1), sin.repeat(b, 1)
+    else:
+        lengths = [7, 300, 1, 129]
+        qkv = torch.randn(1, sum(lengths), 3 * heads * d, generator=gen).to(torch.bfloat16)
+        cos, sin = rope_tables(lengths)
+        rows_cos, rows_sin = cos, sin
+    q, k = pe.apply_rope_bshd(qkv.cuda(), heads, d, cos.cuda(), sin.cuda())
+    assert q.shape == qkv.shape[:-1] + (heads, d) and q.is_contiguous() and k.is_contiguous()
+    flat = qkv.reshape(-1, 3, heads, d)
+    for got, x in ((q, flat[:, 0]), (k, flat[:, 1])):
+        ref = oracle.rope_bshd(x, rows_cos, rows_sin)
+        got = got.reshape(-1, heads, d).cpu()
+        diff = (got.float() - ref.float()).abs()
+        assert (diff <= ref.float().abs() * 2.0 ** -7 + 1e-6).all()  # at most one bf16 rounding apart
+        assert (got != ref).float().mean().item() < 0.01

@@ -121,6 +121,26 @@ def test_rope_validation_without_touching_cuda():
     assert status(rope_cos=32, rope_sin=32, rope_stride_token=64, workspace_bytes=plain_bytes) == -5
 
 
+def test_rope_pass_validation_without_touching_cuda():
+    """pe_b200_rope_qk rejects bad arguments before any CUDA call."""
+    so = _lib.lib()
+
+    def status(**kw):
+        a = dict(q=16, k=16, qst=2304, qsh=64, kst=2304, ksh=64, cos=32, sin=48, tst=64, rows=100, total=100,
+                 heads=12, kv=12, d=64, qo=64, ko=80)
+        a.update(kw)
+        return so.pe_b200_rope_qk(a["q"], a["k"], a["qst"], a["qsh"], a["kst"], a["ksh"], a["cos"], a["sin"], a["tst"],
+                                  a["rows"], a["total"], a["heads"], a["kv"], a["d"], a["qo"], a["ko"], None)
+
+    assert status(d=128) == -8            # head_dim 64 only
+    assert status(q=None) == -1           # NULL input
+    assert status(cos=40) == -3           # misaligned table
+    assert status(qst=2300) == -3         # token stride not a multiple of 16 bytes
+    assert status(tst=32) == -3           # table rows narrower than 64
+    assert status(rows=0) == -2           # no table rows
+    assert status(total=0) == 0           # nothing to do
+
+
 def test_launch_entry_points_reject_null_workspace_without_touching_cuda():
     p = _params()
     so = _lib.lib()

@@ -134,3 +134,29 @@ def test_default_order_prefers_b200_on_sm100(b200):
 
     if torch.cuda.get_device_capability() == (10, 0):
         assert default_order(torch.device("cuda"))[0] == "b200"
+
+
+def test_apply_rope_bshd_matches_reference_kernel(b200):
+    """This library's RoPE pass against the reference's own apply_rope_bshd (CuteDSL,
+    _kernels/rope.py:302-345) on the same packed qkv and per-token tables: same shapes, and the
+    same bf16 values up to rare last-bit differences of the fp32 rotation's rounding."""
+    import packed_encoders_b200 as pe
+
+    try:
+        from packed_encoders._kernels.rope import apply_rope_bshd as ref_rope
+    except Exception as exc:  # noqa: BLE001
+        pytest.skip(f"reference rope kernel unavailable: {type(exc).__name__}")
+    heads, d, total = 12, 64, 1537
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    qkv = torch.randn(1, total, 3 * heads * d, device="cuda", generator=gen).to(torch.bfloat16)
+    pos = torch.arange(total, device="cuda", dtype=torch.float32) % 700
+    inv = 1.0 / 10000.0 ** (torch.arange(0, d, 2, device="cuda", dtype=torch.float32) / d)
+    emb = torch.cat((pos[:, None] * inv, pos[:, None] * inv), -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    q, k = pe.apply_rope_bshd(qkv, heads, d, cos, sin)
+    rq, rk = ref_rope(qkv, heads, d, cos, sin)
+    assert q.shape == rq.shape and k.shape == rk.shape
+    for a, b in ((q, rq), (k, rk)):
+        assert (a.float() - b.float()).abs().max().item() <= 2.0 ** -6 * b.float().abs().max().item()
+        assert (a != b).float().mean().item() < 0.01
+
