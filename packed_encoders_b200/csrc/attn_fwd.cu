@@ -273,9 +273,10 @@ struct Cfg {
   static constexpr int kPass = PASS_ > 0 ? PASS_ : ((BN / SPLIT) < 64 ? BN / SPLIT : 64);
   static constexpr int kThreads = 64 + 128 * SPLIT;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
-  // Head dims above 64 issue their MMAs in groups of four from one elected lane (config 5,
-  // head_dim 256: -4 %); head_dim 64 keeps one elect per MMA (no measurable difference there).
-  static constexpr bool kGroupMma = D > 64;
+  // MMAs go in groups of four (one 64-deep slice) from one lane elected once: P.V always (~1 %
+  // on head_dim 64 workloads), QK for head dims above 64 (config 5, head_dim 256: -4 %; the
+  // head_dim-64 QK measured +2.5 % grouped, within noise, and keeps one elect per MMA).
+  static constexpr bool kGroupQk = D > 64;
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
   static constexpr int kKVPanelBytes = BN * 128;
   static constexpr int kQBytes = kPanels * kQPanelBytes;
@@ -745,25 +746,17 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         mbar_wait(&v_full[st], (int)(j / C::VST) & 1, p.err);
         tc_fence_after();
         const uint32_t v_addr = smem_base + C::kOffV + st * C::kKVBytes;
-        if constexpr (C::kGroupMma) {
 #pragma unroll
-          for (int g = 0; g < C::BN / 64; ++g) {  // groups of four 16-key k-steps
-            uint64_t bdesc[4];
-            uint32_t a_tm[4];
+        for (int g = 0; g < C::BN / 64; ++g) {  // groups of four 16-key k-steps
+          uint64_t bdesc[4];
+          uint32_t a_tm[4];
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const int kk = g * 4 + k4;
-              bdesc[k4] = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
-              a_tm[k4] = tmem + C::col_s(sb) + kk * 8;
-            }
-            mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int kk = g * 4 + k4;
+            bdesc[k4] = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
+            a_tm[k4] = tmem + C::col_s(sb) + kk * 8;
           }
-        } else {
-#pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk) {
-            const uint64_t bdesc = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
-            mma_ts_w(tmem + C::kColO, tmem + C::col_s(sb) + kk * 8, bdesc, idesc_pv, (kk > 0 || !first) ? 1u : 0u);
-          }
+          mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
         }
         // One completion per unit (the epilogue waits on it, so it is committed first): with two
         // S buffers the next unit's QK is issued before this P.V, so S-ready no longer implies
@@ -797,7 +790,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
-          if constexpr (C::kGroupMma) {
+          if constexpr (C::kGroupQk) {
 #pragma unroll
             for (int g = 0; g < C::D / 64; ++g) {  // one 64-column panel: four 16-deep k-steps
               uint64_t adesc[4], bdesc[4];
