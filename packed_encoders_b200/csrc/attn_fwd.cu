@@ -771,17 +771,20 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         pfirst >>= 1;
         plast >>= 1;
       };
-      for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
-        const UnitInfo ui = us.cur;
-        if (ui.n_kv == 0) continue;
+      // Units come from the producer's row slots (published with each Q tile; n_kv < 0 ends the
+      // stream), so this warp reads no schedule data from global memory: no load chain sits
+      // between a unit's last QK and the P.V flush that its epilogue waits for.
+      for (;; ++lu) {
         const int qb = lu % C::QB;
         // The previous unit's last P.Vs go before this unit's first QK: the softmax warps run
         // that unit's epilogue before they can use the new S, so its O is what they wait for.
         while (npend > 0) flush_one();
         mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
         tc_fence_after();
+        const int n_kv = reinterpret_cast<const int*>(smem + C::kOffRows + qb * C::kRowSlotBytes)[4];
+        if (n_kv < 0) break;
         const uint32_t q_addr = smem_base + C::kOffQ + qb * C::kQBytes;
-        for (int t = 0; t < ui.n_kv; ++t, ++i) {
+        for (int t = 0; t < n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
           const int sb = (int)(i % C::NS);
           // With one S buffer the previous P must be consumed first (issue order = execution order).
@@ -812,14 +815,13 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           }
           mma_commit_w(&s_full[sb]);
           mma_commit_w(&k_empty[st]);
-          if (t == ui.n_kv - 1) mma_commit_w(&q_empty[qb]);
+          if (t == n_kv - 1) mma_commit_w(&q_empty[qb]);
           if (npend == 0) pend0 = i;
           pfirst |= (t == 0 ? 1u : 0u) << npend;
-          plast |= (t == ui.n_kv - 1 ? 1u : 0u) << npend;
+          plast |= (t == n_kv - 1 ? 1u : 0u) << npend;
           ++npend;
           if (npend > kLag) flush_one();
         }
-        ++lu;
       }
       while (npend > 0) flush_one();
     }
