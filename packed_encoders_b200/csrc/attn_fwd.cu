@@ -428,34 +428,6 @@ struct UnitInfo {
 };
 
 template <int BN>
-__device__ __forceinline__ UnitInfo unit_info(const AttnParams& p, long long u) {
-  UnitInfo ui;
-  const WorkItem it = p.items[u / p.heads];
-  ui.head = (int)(u % p.heads);
-  ui.kv_head = ui.head / p.group;
-  ui.f = it.seq_first;
-  ui.c = it.seq_count;
-  ui.qb = it.q_block;
-  const int cq0 = p.cu_q[ui.f], cqe = p.cu_q[ui.f + ui.c];
-  ui.q_row0 = cq0 + ui.qb * kTileM;
-  ui.nq = min(kTileM, cqe - ui.q_row0);
-  int kv_lo, kv_hi;
-  if (ui.c == 1) {
-    const int ck0 = p.cu_k[ui.f];
-    int lo, hi;
-    block_key_range(ui.qb, ui.nq, cqe - cq0, p.cu_k[ui.f + 1] - ck0, p.window_left, p.window_right, lo, hi);
-    kv_lo = ck0 + lo;
-    kv_hi = ck0 + hi;
-  } else {
-    kv_lo = p.cu_k[ui.f];
-    kv_hi = p.cu_k[ui.f + ui.c];
-  }
-  ui.kv_lo = kv_lo;
-  ui.n_kv = (ui.nq > 0 && kv_hi > kv_lo) ? (kv_hi - kv_lo + BN - 1) / BN : 0;
-  return ui;
-}
-
-template <int BN>
 __device__ __forceinline__ UnitInfo unit_info_from(const AttnParams& p, const WorkItem& it, long long u) {
   UnitInfo ui;
   ui.head = (int)(u % p.heads);
@@ -482,45 +454,86 @@ __device__ __forceinline__ UnitInfo unit_info_from(const AttnParams& p, const Wo
   return ui;
 }
 
-// Lighter variant for the register-bound softmax warps: only the next work item (16 bytes) is
-// loaded one unit ahead; the segment bounds are read when the unit starts.
-template <int BN>
-struct ItemStream {
-  long long u, n, step;
-  WorkItem nxt;
-  UnitInfo cur;
-  __device__ __forceinline__ ItemStream(const AttnParams& p, long long first, long long n_units, long long stride)
-      : u(first), n(n_units), step(stride) {
-    cur.n_kv = 0;
-    if (u < n) cur = unit_info_from<BN>(p, p.items[u / p.heads], u);
-    if (u + step < n) nxt = p.items[(u + step) / p.heads];
-  }
-  __device__ __forceinline__ bool valid() const { return u < n; }
-  __device__ __forceinline__ void advance(const AttnParams& p) {
-    u += step;
-    if (u < n) cur = unit_info_from<BN>(p, nxt, u);
-    if (u + step < n) nxt = p.items[(u + step) / p.heads];
-  }
-};
+// Segment bounds a unit needs: cu_q[f], cu_q[f + c], cu_k[f], cu_k[f + c] (for one sequence,
+// c = 1, the last two are its key segment).
+__device__ __forceinline__ int4 unit_bounds(const AttnParams& p, const WorkItem& it) {
+  return make_int4(p.cu_q[it.seq_first], p.cu_q[it.seq_first + it.seq_count], p.cu_k[it.seq_first],
+                   p.cu_k[it.seq_first + it.seq_count]);
+}
 
-// The CTA's units (b, b + grid, ...) with the NEXT unit's schedule entry and segment bounds
-// loaded one unit ahead, so their global-load latency hides behind the current unit's work.
+// UnitInfo of unit u from its schedule entry and bounds (arithmetic only; as unit_info).
+template <int BN>
+__device__ __forceinline__ UnitInfo unit_derive(const AttnParams& p, const WorkItem& it, int4 b, uint32_t u) {
+  UnitInfo ui;
+  ui.head = (int)(u % (uint32_t)p.heads);
+  ui.kv_head = ui.head / p.group;
+  ui.f = it.seq_first;
+  ui.c = it.seq_count;
+  ui.qb = it.q_block;
+  ui.q_row0 = b.x + ui.qb * kTileM;
+  ui.nq = min(kTileM, b.y - ui.q_row0);
+  int kv_lo, kv_hi;
+  if (ui.c == 1) {
+    int lo, hi;
+    block_key_range(ui.qb, ui.nq, b.y - b.x, b.w - b.z, p.window_left, p.window_right, lo, hi);
+    kv_lo = b.z + lo;
+    kv_hi = b.z + hi;
+  } else {
+    kv_lo = b.z;
+    kv_hi = b.w;
+  }
+  ui.kv_lo = kv_lo;
+  ui.n_kv = (ui.nq > 0 && kv_hi > kv_lo) ? (kv_hi - kv_lo + BN - 1) / BN : 0;
+  return ui;
+}
+
+template <int BN>
+__device__ __forceinline__ UnitInfo unit_info(const AttnParams& p, long long u) {
+  const WorkItem it = p.items[u / p.heads];
+  return unit_derive<BN>(p, it, unit_bounds(p, it), (uint32_t)u);
+}
+
+// The CTA's units (b, b + grid, ...) for the producer, as a three-stage pipeline so that moving
+// to the next unit waits on no global load: the schedule entry of the unit three ahead and the
+// segment bounds of the unit two ahead are loaded one advance before they are used, and the next
+// unit's UnitInfo is then arithmetic only.
 template <int BN>
 struct UnitStream {
-  long long u, n, step;
+  uint32_t u, n, step;
   UnitInfo cur, nxt;
+  WorkItem it2, it3;  // schedule entries of units u + 2*step, u + 3*step
+  int4 b2;            // bounds of unit u + 2*step
+  __device__ __forceinline__ WorkItem item(const AttnParams& p, uint32_t v) const {
+    return p.items[v / (uint32_t)p.heads];
+  }
   __device__ __forceinline__ UnitStream(const AttnParams& p, long long first, long long n_units, long long stride)
-      : u(first), n(n_units), step(stride) {
+      : u((uint32_t)first), n((uint32_t)n_units), step((uint32_t)stride) {
     cur.n_kv = 0;
     nxt.n_kv = 0;
-    if (u < n) cur = unit_info<BN>(p, u);
-    if (u + step < n) nxt = unit_info<BN>(p, u + step);
+    if (u < n) {
+      const WorkItem it = item(p, u);
+      cur = unit_derive<BN>(p, it, unit_bounds(p, it), u);
+    }
+    if (u + step < n) {
+      const WorkItem it = item(p, u + step);
+      nxt = unit_derive<BN>(p, it, unit_bounds(p, it), u + step);
+    }
+    if (u + 2 * step < n) {
+      it2 = item(p, u + 2 * step);
+      b2 = unit_bounds(p, it2);
+    }
+    if (u + 3 * step < n) it3 = item(p, u + 3 * step);
   }
   __device__ __forceinline__ bool valid() const { return u < n; }
   __device__ __forceinline__ void advance(const AttnParams& p) {
     u += step;
     cur = nxt;
-    if (u + step < n) nxt = unit_info<BN>(p, u + step);
+    if (u + step < n) nxt = unit_derive<BN>(p, it2, b2, u + step);
+    if (u + 2 * step < n) {
+      it2 = it3;
+      b2 = unit_bounds(p, it2);
+    }
+    if (u + 3 * step < n) it3 = item(p, u + 3 * step);
   }
 };
 
