@@ -273,10 +273,8 @@ struct Cfg {
   static constexpr int kPass = PASS_ > 0 ? PASS_ : ((BN / SPLIT) < 64 ? BN / SPLIT : 64);
   static constexpr int kThreads = 64 + 128 * SPLIT;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
-  // MMAs go in groups of four (one 64-deep slice) from one lane elected once: P.V always (~1 %
-  // on head_dim 64 workloads), QK for head dims above 64 (config 5, head_dim 256: -4 %; the
-  // head_dim-64 QK measured +2.5 % grouped, within noise, and keeps one elect per MMA).
-  static constexpr bool kGroupQk = D > 64;
+  // MMAs go in groups of four (one 64-deep slice) from one lane elected once, QK and P.V
+  // (config 5, head_dim 256: -4 %; head_dim 64: config 3 local -3 %, config 2 -1 %).
   static constexpr int kQPanelBytes = kTileM * 128;      // one panel of a 128-row tile
   static constexpr int kKVPanelBytes = BN * 128;
   static constexpr int kQBytes = kPanels * kQPanelBytes;
@@ -806,25 +804,15 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
-          if constexpr (C::kGroupQk) {
 #pragma unroll
-            for (int g = 0; g < C::D / 64; ++g) {  // one 64-column panel: four 16-deep k-steps
-              uint64_t adesc[4], bdesc[4];
+          for (int g = 0; g < C::D / 64; ++g) {  // one 64-column panel: four 16-deep k-steps
+            uint64_t adesc[4], bdesc[4];
 #pragma unroll
-              for (int k4 = 0; k4 < 4; ++k4) {
-                adesc[k4] = sw128_desc(q_addr + g * C::kQPanelBytes + k4 * 32, 16, 1024);
-                bdesc[k4] = sw128_desc(k_addr + g * C::kKVPanelBytes + k4 * 32, 16, 1024);
-              }
-              mma_ss4_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, g > 0 ? 1u : 0u);
+            for (int k4 = 0; k4 < 4; ++k4) {
+              adesc[k4] = sw128_desc(q_addr + g * C::kQPanelBytes + k4 * 32, 16, 1024);
+              bdesc[k4] = sw128_desc(k_addr + g * C::kKVPanelBytes + k4 * 32, 16, 1024);
             }
-          } else {
-#pragma unroll
-            for (int kk = 0; kk < C::D / 16; ++kk) {
-              const uint32_t off = (kk & 3) * 32;
-              const uint64_t adesc = sw128_desc(q_addr + (kk >> 2) * C::kQPanelBytes + off, 16, 1024);
-              const uint64_t bdesc = sw128_desc(k_addr + (kk >> 2) * C::kKVPanelBytes + off, 16, 1024);
-              mma_ss_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
-            }
+            mma_ss4_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, g > 0 ? 1u : 0u);
           }
           mma_commit_w(&s_full[sb]);
           mma_commit_w(&k_empty[st]);
