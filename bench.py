@@ -37,8 +37,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one full-size attn_fwd_kernel launch (config 3
-# global layer, all 512 documents), from the one-pass ncu capture summarised in
-# profiles/attn_fwd_config3_global_traffic.md: 7.54 GB read + 0.903 GB written.
+# global layer, all 512 documents), from a one-pass ncu capture of
+# `python bench.py --case config3-global --iters 2`: 7.54 GB read + 0.903 GB written.
 NCU_TRAFFIC_GLOBAL = 7.54e9 + 0.903e9
 
 
