@@ -102,3 +102,22 @@ def test_attention_leaf_refuses_rectangular_b200(installed):
     q = torch.zeros(1, 2, 10, 64)
     with pytest.raises(UnsupportedTargetError):
         ops.attention(q, q, q, mask=None, window=(-1, -1), scaling=0.125, backend="b200")
+
+
+def test_pieces_replace_attention_and_rope_slots(installed, monkeypatch):
+    """b200_pieces() fills the ModernBERT pieces' BSHD attention and QKV RoPE slots with this
+    library's kernels under the reference's contracts (arch/modernbert_pieces.py:24,38;
+    pieces/rope.py:97-99); the RoPE piece calls apply_rope_bshd with the reference's arguments."""
+    from packed_encoders.pieces.attention import BSHD
+    from packed_encoders.pieces.rope import QKV_BSHD
+
+    from packed_encoders_b200 import ops as b200_ops
+
+    pieces = installed.b200_pieces()
+    assert pieces.attention_bshd.contract == BSHD and "b200" in pieces.attention_bshd.name
+    assert pieces.rope_qkv.contract == QKV_BSHD and "b200" in pieces.rope_qkv.name
+    calls = []
+    monkeypatch.setattr(b200_ops, "apply_rope_bshd", lambda *a: calls.append(a) or ("q", "k"))
+    qkv, cos, sin = torch.zeros(1, 3, 3 * 2 * 64), torch.zeros(3, 64), torch.zeros(3, 64)
+    assert pieces.rope_qkv.execute(qkv, 2, 64, cos, sin) == ("q", "k")
+    assert calls[-1][1:3] == (2, 64)
