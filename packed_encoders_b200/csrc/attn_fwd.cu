@@ -13,12 +13,16 @@
 //     in key tiles of BN tokens; rows mask keys outside their own band.
 //
 // Roles inside one CTA (192 threads):
-//   warp 0        TMA producer: Q tile (double-buffered across units), K/V key tiles (ring)
-//   warp 1        MMA issuer: S = Q K^T (SS form) into a double-buffered TMEM S, then
-//                 O += P V with P read from TMEM (TS form); TMEM allocator
+//   warp 0        TMA producer: Q tile (double-buffered across units), K/V key tiles (rings),
+//                 and each unit's row slot (header + every row's allowed key interval)
+//   warp 1        MMA issuer: S = Q K^T (SS form) into two (or three) TMEM S buffers, then
+//                 O += P V with P read from TMEM (TS form), one or two key tiles behind QK;
+//                 units taken from the row slots; TMEM allocator
 //   warps 2..5    softmax + epilogue: one query row per thread (TMEM lane), exp2 online
 //                 softmax with fp32 row max / sum, bf16 P written back over S, O rescaled in
 //                 TMEM only when the running max grows by more than 2^8, final O / l -> bf16
+// Passes next to it: rope_pass_kernel (rotary tables, before the attention) and
+// gate_pass_kernel (output gate, after it).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
