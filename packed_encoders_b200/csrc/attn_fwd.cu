@@ -260,7 +260,8 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //       P.V, and K runs one key tile ahead of V);  QB Q-tile buffers;
 //   NS  S buffers in TMEM (2: QK of the next key tile overlaps the softmax of this one;
 //       3: QK runs two key tiles ahead of P.V, measured faster for windowed layers and batches
-//       of short sequences, whose units are a few key tiles long; 1: a single S, so two CTAs share an SM and overlap each other);
+//       of short sequences, whose units are a few key tiles long; 1: a single S, so two CTAs
+//       share an SM and overlap each other);
 //   CPS CTAs per SM the configuration is sized for (TMEM columns, shared memory, registers).
 //   POLY of every 16 exp2 pairs evaluated by a cubic on the FMA pipe instead of MUFU (MUFU is the
 //        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
