@@ -19,7 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libpe_b200.so"
 SOURCES = [CSRC / "attn_fwd.cu", CSRC / "noalloc.cu"]
-HEADERS = [ROOT / "include" / "pe_b200_attn.h", CSRC / "sm100_ptx.cuh"]
+HEADERS = [ROOT / "include" / "pe_b200_attn.h", *sorted(CSRC.glob("*.cuh"))]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -260,23 +260,28 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //       P.V, and K runs one key tile ahead of V);  QB Q-tile buffers;
 //   NS  S buffers in TMEM (2: QK of the next key tile overlaps the softmax of this one;
 //       3: QK runs two key tiles ahead of P.V, measured faster for windowed layers and batches
-//       of short sequences, whose units are a few key tiles long; 1: a single S, so two CTAs
-//       share an SM and overlap each other);
+//       of short sequences, whose units are a few key tiles long; 1: a single S, so several
+//       CTAs share an SM and overlap each other);
 //   CPS CTAs per SM the configuration is sized for (TMEM columns, shared memory, registers).
-//   POLY of every 16 exp2 pairs evaluated by a cubic on the FMA pipe instead of MUFU (MUFU is the
-//        softmax bottleneck at head_dim 64: one ex2 per score against 32 scores/clock of MMA).
-//   SPLIT softmax warps per 32-row TMEM lane quarter, each owning 1/SPLIT of the key columns and
-//        of O (more warps to hide latency at the same registers per row).
-template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_, int SPLIT_ = 1, int PASS_ = 0,
-          bool TMA_OUT_ = false, bool GATE_ = false>
+//   POLY of every 16 exp2 pairs evaluated by a cubic on the FMA pipe instead of MUFU.
+//   PASS S columns a softmax thread holds in registers at once (0: min(BN, 64)); a row wider
+//        than PASS is re-read from TMEM for the exp pass.
+//   TMA_OUT windowed-layer epilogue through one TMA store per warp; GATE output gate fused into
+//        the epilogue; STAGE epilogue rows staged through shared memory (head_dim 64).
+//   P_SMEM P goes to shared memory (128B-swizzled, K-major) and P.V reads it from there (SS
+//        MMA) instead of from TMEM. An S buffer is then free as soon as the softmax warps have
+//        loaded it into registers, so the next QK does not wait for this tile's P.V, and a CTA
+//        needs only NS*BN + D TMEM columns (three CTAs per SM at head_dim 64 with NS = 1).
+template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_ = 0, int PASS_ = 0,
+          bool TMA_OUT_ = false, bool GATE_ = false, bool STAGE_ = true, bool P_SMEM_ = false>
 struct Cfg {
+  static constexpr bool kPSmem = P_SMEM_;
   static constexpr bool kGate = GATE_;  // output gate fused into the epilogue (calls with a gate)
-  static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_,
-                       SPLIT = SPLIT_;
-  // S columns a softmax thread holds in registers at once (the row is re-read from TMEM for the
-  // exp pass when it is split into several passes).
-  static constexpr int kPass = PASS_ > 0 ? PASS_ : ((BN / SPLIT) < 64 ? BN / SPLIT : 64);
-  static constexpr int kThreads = 64 + 128 * SPLIT;
+  static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_;
+  static constexpr int kPass = PASS_ > 0 ? PASS_ : (BN < 64 ? BN : 64);
+  static constexpr int kThreads = 192;
+  // Registers per thread that let CPS CTAs share an SM's 64K (allocated in steps of 8).
+  static constexpr int kMaxRegs = (65536 / (kThreads * CPS)) / 8 * 8 > 255 ? 255 : (65536 / (kThreads * CPS)) / 8 * 8;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
   // MMAs go in groups of four (one 64-deep slice) from one lane elected once, QK and P.V
   // (config 5, head_dim 256: -4 %; head_dim 64: config 3 local -3 %, config 2 -1 %).
@@ -287,24 +292,26 @@ struct Cfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + QB * kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
-  static constexpr int kOffBar = kOffV + VST * kKVBytes;
+  // P buffer (P_SMEM): 128 rows x BN keys bf16, BN/64 panels of 128 x 128 B; warp w's 32 rows are
+  // the 4 KB at w * 4096 of each panel, which also serve as that warp's epilogue stage.
+  static constexpr int kPBytes = P_SMEM_ ? kTileM * BN * 2 : 0;
+  static constexpr int kOffP = kOffV + VST * kKVBytes;
+  static constexpr int kOffBar = kOffP + kPBytes;
   // barriers: k_full[ST] k_empty[ST] v_full[VST] v_empty[VST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS]
-  //           o_full row_empty[QB]
-  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1;
+  //           o_full row_empty[QB] (P_SMEM: s_free[NS] p_free)
+  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1 + (P_SMEM_ ? NS + 1 : 0);
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
-  static constexpr int kOffXchg = kOffTmemSlot + 16;  // row max [2][SPLIT][128] and sum [SPLIT][128], fp32
-  static constexpr int kXchgBytes = SPLIT > 1 ? 3 * SPLIT * kTileM * 4 : 0;
   // Epilogue staging (2 KB per softmax warp) so output rows leave as coalesced 128-byte lines;
   // only where shared memory allows (head_dim 64).
-  static constexpr bool kStageOut = (D / SPLIT) == 64 && CPS > 1;
-  // TMA_OUT: with one warp per row, each warp's 32 staged rows leave through one TMA store (4 KB
-  // per warp, 128-byte swizzle: 16-byte chunk c of row r at r*128 + (c ^ r % 8)*16). Measured
-  // faster for windowed layers (config 3 local -9 %) and slower for global layers and query
-  // batches (+2 % / +5 %), so it is chosen per attention kind.
-  static constexpr bool kTmaOut = TMA_OUT_ && kStageOut && SPLIT == 1;
+  static constexpr bool kStageOut = STAGE_ && D == 64 && CPS > 1;
+  // TMA_OUT: each warp's 32 staged rows leave through one TMA store (4 KB per warp, 128-byte
+  // swizzle: 16-byte chunk c of row r at r*128 + (c ^ r % 8)*16). Measured faster for windowed
+  // layers (config 3 local -9 %) and slower for global layers and query batches (+2 % / +5 %),
+  // so it is chosen per attention kind.
+  static constexpr bool kTmaOut = TMA_OUT_ && kStageOut;
   static constexpr int kStageAlign = kTmaOut ? 1024 : 128;  // the 128-byte swizzle needs 1 KB
-  static constexpr int kOffStage = (kOffXchg + kXchgBytes + kStageAlign - 1) & ~(kStageAlign - 1);
-  static constexpr int kStageBytes = kTmaOut ? 4 * 4096 : kStageOut ? 4 * SPLIT * 2048 : 0;
+  static constexpr int kOffStage = (kOffTmemSlot + 16 + kStageAlign - 1) & ~(kStageAlign - 1);
+  static constexpr int kStageBytes = P_SMEM_ ? 0 : kTmaOut ? 4 * 4096 : kStageOut ? 4 * 2048 : 0;
   // Per Q buffer: the unit's header (UnitInfo fields) and every row's allowed key interval,
   // written by the producer so the softmax warps read no schedule data from global memory.
   static constexpr int kRowSlotBytes = 64 + kTileM * 8;
@@ -312,12 +319,15 @@ struct Cfg {
   static constexpr int kSmemBytes = kOffRows + QB * kRowSlotBytes + 1024;  // + align slack
   static constexpr uint32_t kColO = NS * BN;
   static constexpr uint32_t kTmemCols = (kColO + D <= 128) ? 128 : (kColO + D <= 256) ? 256 : 512;
-  // Hold a whole S row in registers only when the register budget allows it.
   static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
   static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
-  static_assert(BN % 64 == 0 && D % 64 == 0 && (BN / SPLIT) % kPass == 0 && kPass % 32 == 0, "tile shape");
-  static_assert((BN / SPLIT) % 32 == 0 && (D / SPLIT) % 32 == 0 && SPLIT <= 2, "column split");
+  static_assert(BN % 64 == 0 && D % 64 == 0 && BN % kPass == 0 && kPass % 32 == 0, "tile shape");
+  static_assert(!P_SMEM_ || (BN == 64 && kPass == 64 && POLY == 0), "P_SMEM: one 64-key panel per S tile");
+  // Epilogue stage of warp w (4 KB, 1 KB aligned): its own rows of the P buffer under P_SMEM.
+  __device__ static constexpr int stage_off(int w) {
+    return P_SMEM_ ? kOffP + w * 4096 : kOffStage + w * (kTmaOut ? 4096 : 2048);
+  }
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
 };
 
@@ -594,7 +604,7 @@ __device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[N *
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::kThreads, C::CPS)
+__global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                     const AttnParams p) {
@@ -611,6 +621,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
   uint64_t* p_full = s_full + C::NS;
   uint64_t* o_full = p_full + C::NS;  // the last P.V of each unit (epilogue)
   uint64_t* row_empty = o_full + 1;    // [QB] the softmax warps took the unit's row slot
+  uint64_t* s_free = row_empty + C::QB;  // [NS] (P_SMEM) the softmax warps hold S in registers
+  uint64_t* p_free = s_free + C::NS;     // (P_SMEM) the P.V reading the P buffer has completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -631,10 +643,14 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     }
     for (int i = 0; i < C::NS; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4 * C::SPLIT);  // one arrival per softmax warp
+      mbar_init(&p_full[i], 4);  // one arrival per softmax warp
     }
     mbar_init(o_full, 1);
-    for (int i = 0; i < C::QB; ++i) mbar_init(&row_empty[i], 4 * C::SPLIT);
+    for (int i = 0; i < C::QB; ++i) mbar_init(&row_empty[i], 4);
+    if constexpr (C::kPSmem) {
+      for (int i = 0; i < C::NS; ++i) mbar_init(&s_free[i], 4);
+      mbar_init(p_free, 1);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -765,19 +781,25 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
 #pragma unroll
         for (int g = 0; g < C::BN / 64; ++g) {  // groups of four 16-key k-steps
           uint64_t bdesc[4];
-          uint32_t a_tm[4];
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const int kk = g * 4 + k4;
-            bdesc[k4] = sw128_desc(v_addr + kk * 16 * 128, C::kKVPanelBytes, 1024);
-            a_tm[k4] = tmem + C::col_s(sb) + kk * 8;
+          for (int k4 = 0; k4 < 4; ++k4) bdesc[k4] = sw128_desc(v_addr + (g * 4 + k4) * 16 * 128, C::kKVPanelBytes, 1024);
+          if constexpr (C::kPSmem) {  // P from the shared-memory P buffer (K-major, like Q)
+            uint64_t adesc[4];
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) adesc[k4] = sw128_desc(smem_base + C::kOffP + g * kTileM * 128 + k4 * 32, 16, 1024);
+            mma_ss4_w(tmem + C::kColO, adesc, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
+          } else {
+            uint32_t a_tm[4];
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) a_tm[k4] = tmem + C::col_s(sb) + (g * 4 + k4) * 8;
+            mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
           }
-          mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
         }
         // One completion per unit (the epilogue waits on it, so it is committed first): with two
         // S buffers the next unit's QK is issued before this P.V, so S-ready no longer implies
         // earlier P.V completions.
         if (last) mma_commit_w(o_full);
+        if constexpr (C::kPSmem) mma_commit_w(p_free);
         mma_commit_w(&v_empty[st]);
       };
       auto flush_one = [&]() {
@@ -803,9 +825,13 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         for (int t = 0; t < n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
           const int sb = (int)(i % C::NS);
-          // With one S buffer the previous P must be consumed first (issue order = execution order).
-          if (C::NS == 1)
+          if constexpr (C::kPSmem) {
+            // The S buffer is reused once the softmax warps hold its previous tile in registers.
+            if (i >= C::NS) mbar_wait(&s_free[sb], (int)((i / C::NS) - 1) & 1, p.err);
+          } else if (C::NS == 1) {
+            // With one S buffer the previous P must be consumed first (issue order = execution order).
             while (npend > 0) flush_one();
+          }
           mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
@@ -833,26 +859,19 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    // SPLIT warps share each 32-row TMEM lane quarter: warp (2 + 4*h + q') owns key columns
-    // [h*BN/SPLIT, (h+1)*BN/SPLIT) of every S tile and O columns [h*D/SPLIT, ...) of rows
-    // 32*q'.. (q' = warp % 4); row maxima and sums are exchanged through shared memory.
-    constexpr int kCols = C::BN / C::SPLIT;     // S columns per thread per key tile
+    // Warp w (2..5) owns TMEM lane quarter w % 4: query rows 32*(w % 4) .. +31, one per thread.
+    constexpr int kCols = C::BN;                // S columns per thread per key tile
     constexpr int kPass = C::kPass;  // S columns held in registers at once
-    constexpr int kOCols = C::D / C::SPLIT;     // O columns per thread
-    const int sw = warp - 2;
-    const int half = sw >> 2;
+    constexpr int kOCols = C::D;                // O columns per thread
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row of this thread == TMEM lane
-    const int col0 = half * kCols;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t o_addr = tmem + lane_base + C::kColO + half * kOCols;
+    const uint32_t o_addr = tmem + lane_base + C::kColO;
     const float NEG_INF = -__int_as_float(0x7f800000);
     const float c2 = p.scale_log2;
-    float* xmax = reinterpret_cast<float*>(smem + C::kOffXchg);     // [2 parity][SPLIT][128]
-    float* xsum = xmax + 2 * C::SPLIT * kTileM;                      // [SPLIT][128]
-    auto pair_sync = [&]() {  // the SPLIT warps of this lane quarter
-      if (C::SPLIT > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(32 * C::SPLIT) : "memory");
-    };
+    // P_SMEM: this thread's row of the P buffer (warp `quarter` owns the 4 KB at quarter * 4096).
+    uint8_t* p_row = smem + C::kOffP + (r >> 3) * 1024 + (r & 7) * 128;
+    bool stage_busy = false;  // a TMA store from this warp's stage may still read it
     long long i = 0;
     int lu = 0;
     for (;; ++lu) {
@@ -879,8 +898,8 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         const int sb = (int)(i % C::NS);
         const uint32_t s_addr = tmem + lane_base + C::col_s(sb);
         const int kt = ui.kv_lo + t * C::BN;
-        // Valid columns of my row, relative to my first column: [c_lo, c_hi).
-        const int c_lo = klo - kt - col0, c_hi = khi - kt - col0;
+        // Valid columns of my row in this key tile: [c_lo, c_hi).
+        const int c_lo = klo - kt, c_hi = khi - kt;
         // Warp-uniform: every lane's row sees all my columns (interior tile), and which of my
         // 32-column chunks hold any allowed key of any lane of this warp.
         // With the whole row in one pass, the S load is issued as soon as S is ready and the
@@ -892,7 +911,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           tc_fence_after();
 #pragma unroll
           for (int cc = 0; cc < kPass / 32; ++cc)
-            tmem_ld32(s_addr + col0 + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+            tmem_ld32(s_addr + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
         }
         const bool full = __all_sync(0xffffffffu, c_lo <= 0 && c_hi >= kCols);
         uint32_t active = 0;
@@ -913,9 +932,14 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
 #pragma unroll
             for (int cc = 0; cc < kPass / 32; ++cc)
               if (active & (1u << (h * (kPass / 32) + cc)))
-                tmem_ld32(s_addr + col0 + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+                tmem_ld32(s_addr + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
           }
           tmem_wait_ld();
+          if constexpr (C::kPSmem) {  // S is in registers: the MMA warp may overwrite the buffer
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[sb]);
+          }
           if (full) {
 #pragma unroll
             for (int j = 0; j + 1 < kPass; j += 2)
@@ -934,15 +958,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
             }
           }
         }
-        float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
-        if (C::SPLIT > 1) {  // combine with the other column halves of my row
-          float* slot = xmax + ((int)(i & 1) * C::SPLIT) * kTileM;
-          slot[half * kTileM + r] = mx;
-          pair_sync();
-#pragma unroll
-          for (int o = 0; o < C::SPLIT; ++o)
-            if (o != half) mx = fmaxf(mx, slot[o * kTileM + r]);
-        }
+        const float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
         const float m_new = fmaxf(m_run, mx * c2);
         const bool need = (m_run != NEG_INF) && (m_new > m_run + kRescaleThreshold);
         const bool any_need = __any_sync(0xffffffffu, need);
@@ -959,7 +975,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
 #pragma unroll
             for (int cc = 0; cc < kPass / 32; ++cc)
               if (active & (1u << (h * (kPass / 32) + cc)))
-                tmem_ld32(s_addr + col0 + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
+                tmem_ld32(s_addr + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
             tmem_wait_ld();
             if (!full) {
 #pragma unroll
@@ -990,7 +1006,25 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
 #pragma unroll
               for (int j = 0; j < 16; ++j) pk[j] = 0u;
             }
-            tmem_st16(s_addr + (col0 + h * kPass + cc * 32) / 2, pk);
+            if constexpr (C::kPSmem) {
+              if (cc == 0) {
+                // The P buffer is free once the previous tile's P.V has completed; a TMA store of
+                // this warp's last epilogue may still be reading these rows.
+                if (i > 0) mbar_wait(p_free, (int)((i - 1) & 1), p.err);
+                if (C::kTmaOut && stage_busy) {
+                  if (lane == 0) bulk_wait_read_all();
+                  __syncwarp();
+                  stage_busy = false;
+                }
+              }
+              // Row r, 16-byte chunk c of the 128B-swizzled K-major tile: r*128 + (c ^ r%8)*16.
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(p_row + (((cc * 4 + c) ^ (r & 7)) << 4)) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            } else {
+              tmem_st16(s_addr + (h * kPass + cc * 32) / 2, pk);
+            }
           }
         }
         // O rescale (rare: the running max grew by more than 2^8) after P is out, so the S
@@ -1017,35 +1051,28 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
         }
         const float2 acc = fadd2(fadd2(accs[0], accs[1]), fadd2(accs[2], accs[3]));
         l_run += acc.x + acc.y;
-        tmem_wait_st();
+        if constexpr (C::kPSmem) fence_proxy_async_smem();  // P stores visible to the tensor core
+        if (!C::kPSmem || any_need) tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[sb]);
       }
-      // Epilogue: O / l -> bf16 rows (my O columns), LSE in natural log.
-      if (C::SPLIT > 1) {  // l is split over the column halves
-        xsum[half * kTileM + r] = l_run;
-        pair_sync();
-        float l_all = 0.f;
-#pragma unroll
-        for (int o = 0; o < C::SPLIT; ++o) l_all += (o == half) ? l_run : xsum[o * kTileM + r];
-        l_run = l_all;
-      }
+      // Epilogue: O / l -> bf16 rows, LSE in natural log.
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       // Gated calls (rows stored by their own thread): the first gate chunk is in flight while
       // the last P.V completes.
-      constexpr int kGateChunk = (C::CPS == 1 && C::SPLIT == 1) ? 8 : 4;  // uint4 per 32*kEpi columns
+      constexpr int kGateChunk = C::CPS == 1 ? 8 : 4;  // uint4 per 32*kEpi columns
       uint4 g_next[(C::kGate && !C::kStageOut) ? kGateChunk : 1];
       if constexpr (C::kGate && !C::kStageOut) {
         if (row_valid && tq < p.total_q) {
 #pragma unroll
-          for (int j = 0; j < kGateChunk; ++j) g_next[j] = load_gate8(p, tq, ui.head, half * kOCols + j * 8);
+          for (int j = 0; j < kGateChunk; ++j) g_next[j] = load_gate8(p, tq, ui.head, j * 8);
         }
       }
       mbar_wait(o_full, lu & 1, p.err);
       tc_fence_after();
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
-      __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head + half * kOCols;
+      __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head;
       if constexpr (C::kTmaOut) {
         // The warp's 32 rows go to its 4 KB stage, then leave with one TMA store; a previous
         // store from the stage must have finished reading it first.
@@ -1054,7 +1081,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
       }
       const bool tma_rows = C::kTmaOut && quarter * 32 + 32 <= ui.nq && ui.q_row0 + quarter * 32 + 32 <= p.total_q;
       if (tma_rows) {
-        uint8_t* stage = smem + C::kOffStage + sw * 4096;
+        uint8_t* stage = smem + C::stage_off(quarter);
         uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
         tmem_ld32(o_addr, oo[0]);
         tmem_ld32(o_addr + 32, oo[1]);
@@ -1080,11 +1107,12 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           else tma_store_3d(&tm_o, stage, 0, ui.head, ui.q_row0 + quarter * 32);
           bulk_commit_group();
         }
+        stage_busy = true;
       } else if constexpr (C::kStageOut) {
         // 64 output columns per thread, in two 32-column halves: each half of all 32 rows of the
         // warp goes through a 2 KB buffer (16-byte chunk c of row r at r*4 + (c ^ (r/2 % 4)),
         // conflict-free both ways) and leaves as 64-byte row segments, 8 rows per instruction.
-        uint4* stage = reinterpret_cast<uint4*>(smem + C::kOffStage + sw * (C::kTmaOut ? 4096 : 2048));
+        uint4* stage = reinterpret_cast<uint4*>(smem + C::stage_off(quarter));
         uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
         tmem_ld32(o_addr, oo[0]);
         tmem_ld32(o_addr + 32, oo[1]);
@@ -1107,16 +1135,16 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
             const int tr = quarter * 32 + row;  // tile row
             const int tok = ui.q_row0 + tr;
             if (tr < ui.nq && tok < p.total_q) {
-              if constexpr (C::kGate) val = gate8(val, load_gate8(p, tok, ui.head, half * kOCols + hh * 32 + c * 8));
+              if constexpr (C::kGate) val = gate8(val, load_gate8(p, tok, ui.head, hh * 32 + c * 8));
               store_out(reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)ui.head * p.o_head +
-                                                 half * kOCols + hh * 32 + c * 8),
+                                                 hh * 32 + c * 8),
                         val);
             }
           }
           __syncwarp();
         }
       } else {
-        constexpr int kEpi = (C::CPS == 1 && C::SPLIT == 1) ? 2 : 1;  // 32-column chunks per TMEM load
+        constexpr int kEpi = C::CPS == 1 ? 2 : 1;  // 32-column chunks per TMEM load
         // Gated calls: the gate of the next 32*kEpi columns is loaded while this chunk is finished.
         static_assert(!C::kGate || kGateChunk == kEpi * 4, "gate chunk");
 #pragma unroll
@@ -1137,7 +1165,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
               if (cc + kEpi < kOCols / 32) {
 #pragma unroll
                 for (int j = 0; j < kEpi * 4; ++j)
-                  g_next[j] = load_gate8(p, tq, ui.head, half * kOCols + (cc + kEpi) * 32 + j * 8);
+                  g_next[j] = load_gate8(p, tq, ui.head, (cc + kEpi) * 32 + j * 8);
               }
             }
 #pragma unroll
@@ -1149,7 +1177,7 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
           }
         }
       }
-      if (store && half == 0 && p.lse != nullptr) {
+      if (store && p.lse != nullptr) {
         const float lse = l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : NEG_INF;
         p.lse[(long long)ui.head * p.total_q + tq] = lse;
       }
@@ -1165,8 +1193,6 @@ __global__ void __launch_bounds__(C::kThreads, C::CPS)
     tmem_dealloc(tmem, C::kTmemCols);
   }
 }
-
-#include "attn_pair.cuh"
 
 // ---------------------------------------------------------------------------------------------
 // Layout probes: one CTA of 128 threads runs a single QK^T or P.V through the same descriptor
@@ -1361,8 +1387,11 @@ static bool make_map_panels(CUtensorMap* map, const void* base, long long tokens
 struct DeviceInfo {
   int sms = 0;
   int supported = -1;
+  int gate_blocks_per_sm = 0;  // resident gate_pass_kernel CTAs per SM (one wave, no tail)
 };
 
+// Per-device facts, looked up once per device under a lock (calls may come from several host
+// threads and devices).
 static DeviceInfo& device_info(int dev) {
   static DeviceInfo infos[64];
   static std::mutex mu;
@@ -1375,40 +1404,44 @@ static DeviceInfo& device_info(int dev) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     d.sms = sms;
     d.supported = (major == 10 && minor == 0) ? 1 : 0;
+    if (d.supported == 1) {
+      int cur = -1, per_sm = 0;
+      cudaGetDevice(&cur);
+      if (cur == dev && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gate_pass_kernel, 256, 0) == cudaSuccess)
+        d.gate_blocks_per_sm = per_sm;
+      cudaGetLastError();
+    }
+    if (d.gate_blocks_per_sm < 1) d.gate_blocks_per_sm = 4;
   }
   return d;
 }
 
 static int block_n_for(int head_dim) { return head_dim == 256 ? 64 : 128; }
 
-// Integer from the environment (tuning knobs), read on every call.
-static int env_int(const char* name, int fallback) {
-  const char* e = getenv(name);
-  return (e && *e) ? atoi(e) : fallback;
-}
-
 // Output gate: a pass of its own after the attention (default), or fused into the attention
-// epilogue (PE_B200_GATE=fused, read on every call). On config 5 shapes (GQA 8/2, causal) the
+// epilogue (PE_B200_GATE=fused, read once per process). On config 5 shapes (GQA 8/2, causal) the
 // pass measured faster at every head dim (64: 3.31 vs 3.43 ms, 128: 4.98 vs 5.10, 256: 7.89 vs
 // 8.25): in the fused form the two MUFU operations per element of the sigmoid run on the softmax
 // warps between one unit and the next, while the pass streams at memory speed.
-static bool gate_as_own_pass(const PeB200AttnParams* p) {
-  const char* e = getenv("PE_B200_GATE");
-  return !(e && strcmp(e, "fused") == 0);
+static bool gate_as_own_pass() {
+  static const bool own_pass = [] {
+    const char* e = getenv("PE_B200_GATE");
+    return !(e && strcmp(e, "fused") == 0);
+  }();
+  return own_pass;
 }
 
-// Host-side choice between the two head_dim-64 kernel layouts (read once).
-static int d64_layout() {
-  static int layout = [] {
-    const char* e = getenv("PE_B200_D64_LAYOUT");
-    if (e && strcmp(e, "2x1") == 0) return 21;   // BN=128, two S buffers, one CTA per SM
-    if (e && strcmp(e, "1x2") == 0) return 12;   // BN=128, one S buffer, two CTAs per SM
-    if (e && strcmp(e, "split") == 0) return 23; // as the default with two softmax warps per row (column halves)
-    if (e && strcmp(e, "pair") == 0) return 31;  // two query tiles per CTA, 128-key tiles, shared K/V
-    return 22;                                    // BN=64, two S buffers, two CTAs per SM, one warp per row
+#ifdef PE_B200_EXPERIMENTS
+// Layout experiments (built only with -DPE_B200_EXPERIMENTS; the shipped library has none):
+// PE_B200_EXP selects a head_dim-64 configuration, read once per process.
+static int experiment() {
+  static const int e = [] {
+    const char* v = getenv("PE_B200_EXP");
+    return (v && *v) ? atoi(v) : 0;
   }();
-  return layout;
+  return e;
 }
+#endif
 
 static long long item_capacity(const PeB200AttnParams* p) {
   return (long long)p->n_seq + (long long)p->total_q / kTileM + 2;
@@ -1476,14 +1509,18 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
       !make_map_panels(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN) ||
       !make_map(&to, p->out, p->total_q, p->heads, C::D, p->o_stride_token, p->o_stride_head, 32))
     return cuda_fail("tensor map encoding", cudaErrorInvalidValue);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (e != cudaSuccess) return cuda_fail("attn_fwd_kernel shared-memory attribute", e);
-    attr_set[dev & 63] = true;
+  {  // the dynamic shared-memory opt-in, once per (configuration, device), under a lock
+    static std::mutex mu;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev & 63]) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(attn_fwd_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+      if (e != cudaSuccess) return cuda_fail("attn_fwd_kernel shared-memory attribute", e);
+      attr_set[dev & 63] = true;
+    }
   }
   AttnParams ap;
   ap.cu_q = p->cu_seqlens_q;
@@ -1509,47 +1546,6 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   const int grid = (int)(units < slots ? units : slots);
   attn_fwd_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, to, ap);
   return launch_status("attn_fwd_kernel launch");
-}
-
-template <class C>
-static int launch_pair(const PeB200AttnParams* p, cudaStream_t stream, int sms) {
-  CUtensorMap tq, tk, tv;
-  if (!make_map(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
-      !make_map(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
-      !make_map(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN))
-    return cuda_fail("tensor map encoding", cudaErrorInvalidValue);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(attn_pair_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (e != cudaSuccess) return cuda_fail("attn_pair_kernel shared-memory attribute", e);
-    attr_set[dev & 63] = true;
-  }
-  AttnParams ap;
-  ap.cu_q = p->cu_seqlens_q;
-  ap.cu_k = p->cu_seqlens_k;
-  ap.heads = p->heads;
-  ap.group = p->heads / p->kv_heads;
-  ap.total_q = p->total_q;
-  ap.out = static_cast<__nv_bfloat16*>(p->out);
-  ap.o_tok = p->o_stride_token;
-  ap.o_head = p->o_stride_head;
-  ap.lse = p->lse;
-  ap.scale_log2 = p->scale * 1.4426950408889634f;
-  ap.window_left = p->window_left;
-  ap.window_right = p->causal ? 0 : p->window_right;
-  ap.header = static_cast<const WsHeader*>(p->workspace);
-  ap.items = reinterpret_cast<const WorkItem*>(static_cast<const uint8_t*>(p->workspace) + kHeaderBytes);
-  ap.err = &static_cast<WsHeader*>(p->workspace)->error;
-  ap.gate = static_cast<const __nv_bfloat16*>(p->gate);
-  ap.g_tok = p->g_stride_token;
-  ap.g_head = p->g_stride_head;
-  const long long pairs = ((item_capacity(p) + 1) / 2) * p->heads;
-  const int grid = (int)(pairs < sms ? pairs : sms);
-  attn_pair_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, ap);
-  return launch_status("attn_pair_kernel launch");
 }
 
 }  // namespace pe_b200
@@ -1647,16 +1643,12 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
     r.k_stride_head = 64;
     return pe_b200_attn_run(&r, stream);
   }
-  if (p->gate && gate_as_own_pass(p)) {
+  if (p->gate && gate_as_own_pass()) {
     PeB200AttnParams ungated = *p;
     ungated.gate = nullptr;
     st = pe_b200_attn_run(&ungated, stream);
     if (st != PE_B200_OK) return st;
-    static int per_sm = 0;  // resident 256-thread CTAs per SM (registers bound it): one wave, no tail
-    if (per_sm == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gate_pass_kernel, 256, 0) != cudaSuccess)
-      per_sm = 4;
-    if (per_sm < 1) per_sm = 1;
-    const long long slots = (long long)info.sms * per_sm;
+    const long long slots = (long long)info.sms * info.gate_blocks_per_sm;
     const int grid = (int)(p->total_q < slots ? p->total_q : slots);
     gate_pass_kernel<<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(p->out), static_cast<const __nv_bfloat16*>(p->gate),
                                           p->total_q, p->heads, p->head_dim / 8, p->o_stride_token, p->o_stride_head,
@@ -1665,32 +1657,37 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   }
   if (p->gate) {  // output gate fused: separate instantiations, so ungated kernels carry no gate code
     switch (p->head_dim) {
-      case 64: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1, 0, false, true>>(p, s, info.sms);
-      case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4, 1, 0, false, true>>(p, s, info.sms);
-      case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 1, 0, false, true>>(p, s, info.sms);
+      case 64: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 0, false, true>>(p, s, info.sms);
+      case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4, 0, false, true>>(p, s, info.sms);
+      case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 0, false, true>>(p, s, info.sms);
       default: return PE_B200_ERR_UNSUPPORTED;
     }
   }
   switch (p->head_dim) {
-    case 64:
-      // Layouts of the same kernel (PE_B200_D64_LAYOUT): default 64-key tiles, two S buffers and
-      // two CTAs per SM; 2x1 / 1x2 are the 128-key-tile variants kept for comparison.
-      if (d64_layout() == 21) return launch_attention<Cfg<64, 128, 3, 3, 2, 2, 1, 8>>(p, s, info.sms);
-      if (d64_layout() == 12) return launch_attention<Cfg<64, 128, 2, 2, 2, 1, 2, 0>>(p, s, info.sms);
-      if (d64_layout() == 23) return launch_attention<Cfg<64, 64, 4, 4, 2, 2, 2, 0, 2>>(p, s, info.sms);
-      if (d64_layout() == 31) return launch_pair<PairCfg<128, 4, 3, 2, 64>>(p, s, info.sms);
-      switch (env_int("PE_B200_D64_POLY", 0)) {  // tuning knob: exp2 pairs (of 16) on the FMA pipe
-        case 4: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 4, 1>>(p, s, info.sms);
-        case 8: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 8, 1>>(p, s, info.sms);
-        default:
-          if ((p->window_left >= 0 || p->window_right >= 0) && !p->causal)
-            return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 1, 0, true>>(p, s, info.sms);
-          // Batches of short sequences (query batches: units of one or two key tiles) also run
-          // P.V two tiles behind QK (config 2 -2.3 %); long global sequences measured +1.4 % so.
-          if (p->max_seqlen_k > 0 && p->max_seqlen_k <= kTileM)
-            return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 1>>(p, s, info.sms);
-          return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 1>>(p, s, info.sms);
+    case 64: {
+      const bool windowed = (p->window_left >= 0 || p->window_right >= 0) && !p->causal;
+#ifdef PE_B200_EXPERIMENTS
+      switch (experiment()) {
+        case 1: return launch_attention<Cfg<64, 64, 2, 2, 1, 1, 4, 0, 32, false, false, false>>(p, s, info.sms);
+        case 2: return launch_attention<Cfg<64, 64, 2, 2, 1, 1, 4, 0, 64, false, false, false>>(p, s, info.sms);
+        case 3: return launch_attention<Cfg<64, 64, 3, 3, 1, 1, 3, 0, 32, false, false, false>>(p, s, info.sms);
+        case 4: return launch_attention<Cfg<64, 64, 3, 3, 1, 1, 3, 0, 64, false, false, false>>(p, s, info.sms);
+        case 5: return launch_attention<Cfg<64, 64, 3, 2, 1, 1, 3, 0, 64>>(p, s, info.sms);
+        case 6: return launch_attention<Cfg<64, 64, 3, 2, 1, 1, 3, 0, 0, false, false, true, true>>(p, s, info.sms);
+        case 7: return launch_attention<Cfg<64, 64, 2, 2, 1, 1, 3, 0, 0, false, false, true, true>>(p, s, info.sms);
+        case 8: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 0, false, false, true, true>>(p, s, info.sms);
+        case 9: return launch_attention<Cfg<64, 64, 3, 2, 1, 1, 3, 0, 0, true, false, true, true>>(p, s, info.sms);
+        default: break;
       }
+#endif
+      // 64-key tiles, two CTAs per SM. Windowed layers: three S buffers and the TMA-store
+      // epilogue. Batches of short sequences (query batches: units of one or two key tiles) also
+      // run P.V two tiles behind QK (config 2 -2.3 %); long global sequences measured +1.4 % so.
+      if (windowed) return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 0, true>>(p, s, info.sms);
+      if (p->max_seqlen_k > 0 && p->max_seqlen_k <= kTileM)
+        return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2>>(p, s, info.sms);
+      return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2>>(p, s, info.sms);
+    }
     case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4>>(p, s, info.sms);
     case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0>>(p, s, info.sms);
     default: return PE_B200_ERR_UNSUPPORTED;

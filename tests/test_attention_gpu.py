@@ -26,20 +26,31 @@ def _b200():
     return pe
 
 
-def _assert_parity(got: torch.Tensor, ref: torch.Tensor, what: str = "", value_std: float = 1.0):
-    """MAX_ABS is the bar for unit-variance values (runtime/attention.py:40); the error of the
-    bf16-P strategy (shared with triton_packed_attention.py:129-132) scales with |v|, so inputs
-    with a larger value spread get the bar times their standard deviation."""
+def _assert_parity(got: torch.Tensor, ref: torch.Tensor, what: str = ""):
+    """The north-star bars, unscaled: max-abs <= 2e-2 and per-token cosine >= 0.9999 against the
+    fp32 CPU path. Prints the observed errors so parity can be read off the test log."""
     got = got.float().cpu()
     ref = ref.float().cpu()
     assert torch.isfinite(got).all(), f"{what}: non-finite output"
     err = (got - ref).abs().max().item() if got.numel() else 0.0
-    bar = MAX_ABS * max(1.0, value_std)
-    assert err <= bar, f"{what}: max abs err {err:.3g} > {bar:.3g}"
+    cos_min = 1.0
     if got.numel():
         cos = torch.nn.functional.cosine_similarity(got.flatten(1), ref.flatten(1), dim=1)
-        # a zero row (never produced for valid rows) would give cos 0; all rows here are real
-        assert cos.min().item() >= MIN_COS, f"{what}: min per-token cosine {cos.min().item():.6f}"
+        cos_min = cos.min().item()
+    print(f"PARITY {what}: max_abs={err:.5f} min_cos={cos_min:.7f}")
+    assert err <= MAX_ABS, f"{what}: max abs err {err:.3g} > {MAX_ABS}"
+    # a zero row (never produced for valid rows) would give cos 0; all rows here are real
+    assert cos_min >= MIN_COS, f"{what}: min per-token cosine {cos_min:.6f}"
+    return err, cos_min
+
+
+def _assert_lse(got: torch.Tensor, ref: torch.Tensor, what: str = ""):
+    got, ref = got.float().cpu(), ref.float().cpu()
+    finite = torch.isfinite(ref)
+    assert torch.equal(finite, torch.isfinite(got)), f"{what}: LSE finiteness differs"
+    err = (got[finite] - ref[finite]).abs().max().item() if finite.any() else 0.0
+    print(f"PARITY {what}: lse_max_abs={err:.6f}")
+    assert err <= LSE_ATOL, f"{what}: LSE max abs err {err:.3g} > {LSE_ATOL}"
 
 
 def _run(q, k, v, cu, *, scale, window=(-1, -1), causal=False, cu_k=None):
@@ -80,17 +91,54 @@ def test_layout_probe_pv(dim):
     torch.testing.assert_close(o, ref, atol=1e-3, rtol=1e-4)
 
 
-@pytest.mark.parametrize("name", golden_names())
+# Rounding the EXACT fp32 reference output of this fixture to bf16 already moves it by 0.0221
+# (q, k, v scaled by 2 as in tests/test_cpu_short_attention.py:198; |out| reaches 8.1, where half
+# a bf16 ulp is 0.031): no bf16 output, however computed, meets 2e-2 absolute on it. Measured on
+# B200: this kernel 0.0221, FlashAttention-2 varlen (the reference's compiled-FA path) 0.0221.
+# test_golden_vectors_no_worse_than_fa2 checks every fixture, this one included, against FA2.
+_BF16_QUANTUM_BOUND = {
+    "native_edge_half15": "bf16 rounding of the exact output alone is 0.0221 > 2e-2 (|out| up to 8.1); "
+                          "measured: this kernel 0.0221, FA2 varlen 0.0221",
+}
+
+
+def _golden_params():
+    return [pytest.param(n, marks=pytest.mark.xfail(strict=True, reason=_BF16_QUANTUM_BOUND[n]))
+            if n in _BF16_QUANTUM_BOUND else n for n in golden_names()]
+
+
+def _run_golden(g):
+    return _run(g["q"], g["k"], g["v"], g["cu_q"], scale=g["scale"], window=g["window"], causal=g["causal"],
+                cu_k=None if torch.equal(g["cu_q"], g["cu_k"]) else g["cu_k"])
+
+
+@pytest.mark.parametrize("name", _golden_params())
 def test_golden_vectors(name):
     g = load_golden(name)
-    out, lse = _run(g["q"], g["k"], g["v"], g["cu_q"], scale=g["scale"], window=g["window"], causal=g["causal"],
-                    cu_k=None if torch.equal(g["cu_q"], g["cu_k"]) else g["cu_k"])
-    # native_edge_* fixtures scale q, k, v by 2 (tests/test_cpu_short_attention.py:198):
-    # emulating the bf16-P rounding on CPU gives the same 0.0221 max error there.
-    _assert_parity(out, g["out"], name, value_std=g["v"].float().std().item())
+    out, lse = _run_golden(g)
     _, ref_lse = oracle.attention_prefixed(g["q"], g["k"], g["v"], g["cu_q"], g["cu_k"], scale=g["scale"],
                                            window=g["window"], causal=g["causal"])
-    torch.testing.assert_close(lse.cpu(), ref_lse, atol=LSE_ATOL, rtol=0)
+    _assert_lse(lse, ref_lse, name)
+    _assert_parity(out, g["out"], name)
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_vectors_no_worse_than_fa2(name):
+    """Against the reference's compiled GPU path on the same fixture: FlashAttention-2 varlen
+    (packed_encoders/ops.py:364-371; the FA4 build the reference prefers on sm_100 is not in this
+    image). Its bf16 output has the same quantum as ours, so its error is the yardstick for the
+    fixtures whose exact outputs are too large for a 2e-2 absolute bar."""
+    fa = pytest.importorskip("flash_attn")
+    g = load_golden(name)
+    out, _ = _run_golden(g)
+    lq = int((g["cu_q"][1:] - g["cu_q"][:-1]).max())
+    lk = int((g["cu_k"][1:] - g["cu_k"][:-1]).max())
+    ref_fa = fa.flash_attn_varlen_func(g["q"].cuda(), g["k"].cuda(), g["v"].cuda(), g["cu_q"].cuda(), g["cu_k"].cuda(),
+                                       lq, lk, softmax_scale=g["scale"], causal=g["causal"], window_size=g["window"])
+    ours = (out.float().cpu() - g["out"]).abs().max().item()
+    theirs = (ref_fa.float().cpu() - g["out"]).abs().max().item()
+    print(f"PARITY {name}: max_abs={ours:.5f} fa2_max_abs={theirs:.5f}")
+    assert ours <= theirs + 1e-3, f"{name}: {ours:.4g} vs FA2 {theirs:.4g}"
 
 
 CASES = [
@@ -117,8 +165,48 @@ def test_matches_oracle(lengths, heads, kv_heads, dim, window, causal):
     scale = dim ** -0.5
     out, lse = _run(q, k, v, cu, scale=scale, window=window, causal=causal)
     ref, ref_lse = oracle.attention(q, k, v, cu, scale=scale, window=window, causal=causal)
-    _assert_parity(out, ref, f"{lengths[:6]} H{heads}/{kv_heads} D{dim} w{window} c{causal}")
-    torch.testing.assert_close(lse.cpu(), ref_lse, atol=LSE_ATOL, rtol=0)
+    what = f"{lengths[:6]} H{heads}/{kv_heads} D{dim} w{window} c{causal}"
+    _assert_parity(out, ref, what)
+    _assert_lse(lse, ref_lse, what)
+
+
+@pytest.mark.parametrize("window", [(-1, -1), (64, 64)])
+def test_attention_bshd_drop_in(window):
+    """ops.attention_bshd's packed form (packed_encoders/ops.py:502-538): [1, T, H, D] views in
+    (q, k contiguous from the RoPE pass, v a strided slice of the fused qkv, forward.py:197-205),
+    [1, T, H*D] out, against the oracle."""
+    pe = _b200()
+    lengths, heads = [40, 300, 7, 129, 513], 12
+    total = sum(lengths)
+    gen = torch.Generator().manual_seed(23)
+    qkv = torch.randn(1, total, 3, heads, 64, generator=gen).to(torch.bfloat16)
+    cu = torch.tensor([0] + lengths, dtype=torch.int32).cumsum(0, dtype=torch.int32)
+    q, k = qkv[:, :, 0].contiguous(), qkv[:, :, 1].contiguous()
+    dq, dk, dqkv = q.cuda(), k.cuda(), qkv.cuda()
+    out = pe.attention_bshd(dq, dk, dqkv[:, :, 2], window=window, scaling=0.125, cu_seqlens=cu.cuda(),
+                            max_seqlen=max(lengths))
+    torch.cuda.synchronize()
+    assert out.shape == (1, total, heads * 64)
+    ref, _ = oracle.attention(q[0], k[0], qkv[0, :, 2], cu, scale=0.125, window=window)
+    _assert_parity(out.view(total, heads, 64), ref, f"attention_bshd w{window}")
+
+
+@pytest.mark.parametrize("window", [(-1, -1), (64, 64)])
+def test_flash_attention_varlen_drop_in(window):
+    """ops.flash_attention_varlen (packed_encoders/ops.py:432-461): [1, H, T, D] head-major views
+    in (the transposed path), [1, T, H*D] out, against the oracle."""
+    pe = _b200()
+    lengths, heads = [65, 1, 200, 33, 400], 8
+    total = sum(lengths)
+    gen = torch.Generator().manual_seed(29)
+    q, k, v = (torch.randn(1, heads, total, 64, generator=gen).to(torch.bfloat16) for _ in range(3))
+    cu = torch.tensor([0] + lengths, dtype=torch.int32).cumsum(0, dtype=torch.int32)
+    out = pe.flash_attention_varlen(q.cuda(), k.cuda(), v.cuda(), cu.cuda(), max(lengths), window, 0.125)
+    torch.cuda.synchronize()
+    assert out.shape == (1, total, heads * 64)
+    ref, _ = oracle.attention(q[0].transpose(0, 1), k[0].transpose(0, 1), v[0].transpose(0, 1), cu, scale=0.125,
+                              window=window)
+    _assert_parity(out.view(total, heads, 64), ref, f"flash_attention_varlen w{window}")
 
 
 @pytest.mark.parametrize("logit_scale", [0.01, 1.0, 8.0])
@@ -201,33 +289,6 @@ def test_schedule_covers_every_block_once_with_sequences_contiguous(window, caus
         else:
             group_cost[-1] = max(group_cost[-1], cost)
     assert group_cost == sorted(group_cost, reverse=True)
-
-
-def test_pair_layout_matches_oracle_in_subprocess():
-    """The opt-in two-tiles-per-CTA layout (PE_B200_D64_LAYOUT=pair, read once per process) on
-    global, windowed, causal and packed-short cases."""
-    import subprocess
-    import sys
-    from pathlib import Path
-
-    code = r"""
-import torch, oracle, packed_encoders_b200 as pe
-from conftest import packed_inputs
-for lengths, window, causal in [([300, 7, 129, 1000], (-1, -1), False), ([700, 40, 33, 260], (64, 64), False),
-                                ([513, 64, 65], (-1, -1), True), ([30] * 40 + [5, 100], (-1, -1), False)]:
-    q, k, v, cu = packed_inputs(lengths, 3, 64, seed=11)
-    out = pe.packed_attention(q.cuda(), k.cuda(), v.cuda(), cu.cuda(), max(lengths), scale=0.125, window=window,
-                              causal=causal)
-    ref, _ = oracle.attention(q.float(), k.float(), v.float(), cu, scale=0.125, window=window, causal=causal)
-    err = (out.float().cpu() - ref).abs().max().item()
-    assert err < 2e-2, (lengths, window, causal, err)
-assert pe.device_error_word() == 0
-print("ok")
-"""
-    root = Path(__file__).resolve().parents[1]
-    env = {**__import__("os").environ, "PE_B200_D64_LAYOUT": "pair", "PYTHONPATH": f"{root}:{root / 'tests'}"}
-    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
-    assert res.returncode == 0 and "ok" in res.stdout, res.stderr[-2000:]
 
 
 @pytest.mark.parametrize("mode", ["pass", "fused"])
