@@ -159,13 +159,26 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream);
  * device memory at start-up and allows no allocation per request. p->workspace and
  * p->workspace_bytes are ignored; the tile schedule and error word live in a fixed 1 MiB
  * array inside the library's device memory (held on every GPU that loads the library until
- * the process exits). Limit: n_seq + total_q / 128 + 2 <= 65,520, else
- * PE_B200_ERR_SCRATCH_LIMIT and nothing is enqueued. The first call on a device looks up the
- * array's address with that device current; make it before any stream capture. All calls
- * share the array, so calls that overlap on the GPU race: serialise them. Nothing here
- * allocates. This entry point has no counterpart in the reference.
+ * the process exits). Limit: pe_b200_attn_workspace_size(p) <= 1 MiB, else
+ * PE_B200_ERR_SCRATCH_LIMIT and nothing is enqueued; without rotary tables that is
+ * n_seq + total_q / 128 + 2 <= 65,520, and a rotary call also needs room for its rotated q and
+ * k, so only small rotary calls fit. The first call on a device (and the first after its
+ * context was re-created, e.g. by cudaDeviceReset) looks up the array's address with that
+ * device current; make it before any stream capture. All calls share the array, so calls that
+ * overlap on the GPU race: serialise them. Device-side errors of the last call are read with
+ * pe_b200_noalloc_error_word. Nothing here allocates. This entry point has no counterpart in
+ * the reference.
  */
 int pe_b200_attn_fwd_noalloc(const PeB200AttnParams* p, void* stream);
+
+/*
+ * The device error word (PE_B200_DEVERR_* bits) of the last pe_b200_attn_fwd_noalloc call on
+ * the current device, copied into *out with one copy on `stream` (ordered after the calls
+ * enqueued there) and a wait for it; 0 when that call saw no bounded-wait timeout, schedule
+ * overflow or malformed cu_seqlens. Allocates nothing. No counterpart in the reference (it is
+ * the no-allocation path's view of the workspace error word of pe_b200_attn_fwd).
+ */
+int pe_b200_noalloc_error_word(int* out, void* stream);
 
 /*
  * Rotary embedding of q and k into contiguous copies, the reference's BSHD RoPE pass

@@ -35,11 +35,14 @@ _ptr = ctypes.c_void_p
 
 def build(reference: bool | None = None) -> None:
     """Compile the oracle (and the reference kernel when the reference tree exists)."""
+    from oracle.reference_tree import reference_dir
+
     targets = ["all"]
+    tree = reference_dir()
     if reference is None:
-        reference = Path("/root/reference/packed_encoders/cpu/local_attention_x86.c").exists()
+        reference = tree is not None and (tree / "packed_encoders/cpu/local_attention_x86.c").exists()
     if reference:
-        targets.append("ref")
+        targets += ["ref", f"REFERENCE={tree}"]
     subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
 
 

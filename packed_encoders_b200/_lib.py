@@ -44,7 +44,8 @@ class PeB200AttnParams(ctypes.Structure):
 EXPORTS = (
     "pe_b200_abi_version", "pe_b200_status_string", "pe_b200_last_error_detail", "pe_b200_device_supported",
     "pe_b200_attn_workspace_size", "pe_b200_attn_fwd", "pe_b200_build_schedule", "pe_b200_attn_run",
-    "pe_b200_debug_qk", "pe_b200_debug_pv", "pe_b200_rope_qk",
+    "pe_b200_debug_qk", "pe_b200_debug_pv", "pe_b200_rope_qk", "pe_b200_attn_fwd_noalloc",
+    "pe_b200_noalloc_error_word",
 )
 
 
@@ -73,6 +74,10 @@ def lib() -> ctypes.CDLL:
         fn = getattr(so, name)
         fn.restype = ctypes.c_int
         fn.argtypes = [ctypes.POINTER(PeB200AttnParams), _p]
+    so.pe_b200_attn_fwd_noalloc.restype = ctypes.c_int
+    so.pe_b200_attn_fwd_noalloc.argtypes = [ctypes.POINTER(PeB200AttnParams), _p]
+    so.pe_b200_noalloc_error_word.restype = ctypes.c_int
+    so.pe_b200_noalloc_error_word.argtypes = [ctypes.POINTER(ctypes.c_int), _p]
     so.pe_b200_rope_qk.restype = ctypes.c_int
     so.pe_b200_rope_qk.argtypes = [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _i32, _i32, _i32, _p, _p, _p]
     so.pe_b200_debug_qk.restype = ctypes.c_int

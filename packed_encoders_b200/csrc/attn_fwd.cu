@@ -1568,7 +1568,8 @@ const char* pe_b200_status_string(int status) {
     case PE_B200_ERR_CUDA: return "a CUDA launch or tensor-map call failed";
     case PE_B200_ERR_UNSUPPORTED: return "head_dim must be 64, 128 or 256";
     case PE_B200_ERR_SCRATCH_LIMIT:
-      return "call too large for the fixed 1 MiB no-allocation scratch (n_seq + total_q/128 + 2 > 65520)";
+      return "call too large for the fixed 1 MiB no-allocation scratch (workspace size > 1 MiB; without rotary "
+             "tables: n_seq + total_q/128 + 2 > 65520)";
     default: return "unknown status";
   }
 }

@@ -16,6 +16,14 @@ After ``install()``, the reference's own entry points run on the B200 kernels un
   packed / padded / prefixed forms, first in the default order on sm_100, and the Qwen3.5
   engine accepts ``attention_backend="b200"`` (arch/qwen3_5/__init__.py:49).
 
+* on an sm_100 GPU (B200 / GB200), the default and ``"auto"`` backends resolve to ``"b200"``:
+  ``pack._default_backend`` (pack.py:147-158), ``pack._resolve_attention_backend``
+  (pack.py:161-192) and ``forward._resolve_eager_backend`` (forward.py:301-331, the branch that
+  consults the calibrated Triton-vs-FA policy of attention_dispatch.py:129-205, eager and
+  ``for_cuda_graph`` alike) stop there, so ``pe.pack(model)`` with no backend argument runs on
+  these kernels. Training (grad enabled) keeps the reference's own resolution: the kernels are
+  forward-only, like the Triton kernel they replace.
+
 There is no policy and no fallback: ``"b200"`` always means these kernels; anything they do
 not implement raises ``UnsupportedTargetError``.
 """
@@ -107,6 +115,23 @@ def b200_candidate(window, scale):
     return packed, padded, prefixed
 
 
+# --------------------------------------------------------------------------- device policy
+def on_b200() -> bool:
+    """True when the current CUDA device is an sm_100 part these kernels run on. Uses the
+    reference's own capability probe (attention_dispatch.py:148-154), so a test can fake it."""
+    from packed_encoders import attention_dispatch
+
+    return attention_dispatch.current_compute_capability() == (10, 0)
+
+
+def resolve_backend(backend: str | None) -> str | None:
+    """The single policy that replaces the calibrated Triton-vs-FA dispatch on sm_100: an unset
+    or ``"auto"`` backend, in inference, is ``"b200"``. Anything else is returned unchanged."""
+    if backend in (None, "auto") and not torch.is_grad_enabled() and on_b200():
+        return BACKEND
+    return backend
+
+
 # --------------------------------------------------------------------------- install
 def install() -> None:
     """Patch the imported reference package in place (idempotent)."""
@@ -117,6 +142,7 @@ def install() -> None:
     forward = importlib.import_module("packed_encoders.forward")
     ops = importlib.import_module("packed_encoders.ops")
     pack = importlib.import_module("packed_encoders.pack")  # the package re-exports a function of this name
+    graph = importlib.import_module("packed_encoders.graph")
     rt_attention = importlib.import_module("packed_encoders.runtime.attention")
 
     orig_use_bshd = ops.use_bshd_rope_flash
@@ -152,6 +178,7 @@ def install() -> None:
 
     @functools.wraps(orig_fused)
     def fused_forward(model, params, input_ids, attention_mask, *, execution=None, backend="sdpa"):
+        backend = resolve_backend(backend) if backend == "auto" else backend
         if backend == BACKEND:  # always the packed path, like the Triton backend (forward.py:696-703)
             if attention_mask is None:
                 attention_mask = torch.ones_like(input_ids)
@@ -159,11 +186,48 @@ def install() -> None:
                                            execution=execution)
         return orig_fused(model, params, input_ids, attention_mask, execution=execution, backend=backend)
 
+    orig_resolve_eager = forward._resolve_eager_backend
+
+    @functools.wraps(orig_resolve_eager)
+    def _resolve_eager_backend(backend, workload=None, *, triton_supported=False, flash_available=None,
+                               for_cuda_graph=False):
+        if backend == BACKEND:
+            return BACKEND
+        if backend == "auto" and resolve_backend(backend) == BACKEND:
+            return BACKEND  # the calibrated Triton-vs-FA policy is not consulted on sm_100
+        return orig_resolve_eager(backend, workload, triton_supported=triton_supported,
+                                  flash_available=flash_available, for_cuda_graph=for_cuda_graph)
+
+    orig_default = pack._default_backend
+
+    @functools.wraps(orig_default)
+    def _default_backend():
+        return BACKEND if on_b200() else orig_default()
+
+    orig_resolve_attention = pack._resolve_attention_backend
+
+    @functools.wraps(orig_resolve_attention)
+    def _resolve_attention_backend(backend):
+        if backend == BACKEND or (backend == "auto" and on_b200()):
+            return BACKEND
+        return orig_resolve_attention(backend)
+
+    orig_rect = graph.rectangular_graph_backend
+
+    @functools.wraps(orig_rect)
+    def rectangular_graph_backend(backend):
+        # b200 serves the packed path only: padded batches reach it through the packed runner.
+        return None if backend == BACKEND else orig_rect(backend)
+
     orig_prepare = pack._prepare_modernbert
 
     @functools.wraps(orig_prepare)
     def _prepare_modernbert(encoder, *, attention_backend=None, cuda_graph=None, cuda_graph_seq_cutoff=64,
                             **kwargs):
+        if attention_backend is None:
+            attention_backend = pack._default_backend()
+        if attention_backend == "auto" and on_b200():
+            attention_backend = BACKEND
         if attention_backend != BACKEND:
             return orig_prepare(encoder, attention_backend=attention_backend, cuda_graph=cuda_graph,
                                 cuda_graph_seq_cutoff=cuda_graph_seq_cutoff, **kwargs)
@@ -180,7 +244,11 @@ def install() -> None:
     ops.attention_bshd = attention_bshd
     ops.attention = attention
     forward.fused_forward = fused_forward
+    forward._resolve_eager_backend = _resolve_eager_backend
+    pack._default_backend = _default_backend
+    pack._resolve_attention_backend = _resolve_attention_backend
     pack._prepare_modernbert = _prepare_modernbert
+    graph.rectangular_graph_backend = rectangular_graph_backend
 
     rt_attention._CANDIDATES[BACKEND] = b200_candidate
     orig_order = rt_attention.default_order
@@ -209,4 +277,5 @@ def install() -> None:
     _INSTALLED["done"] = True
 
 
-__all__ = ["BACKEND", "b200_attention_bshd_piece", "b200_candidate", "b200_pieces", "b200_rope_qkv_piece", "install"]
+__all__ = ["BACKEND", "b200_attention_bshd_piece", "b200_candidate", "b200_pieces", "b200_rope_qkv_piece", "install",
+           "on_b200", "resolve_backend"]

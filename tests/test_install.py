@@ -6,18 +6,12 @@ The reference's own tests do the same with monkeypatched loaders
 
 from __future__ import annotations
 
-import sys
-from pathlib import Path
-
 import pytest
 import torch
 
-ROOT = Path(__file__).resolve().parents[1]
-for candidate in (ROOT / "baseline" / "_ref", Path("/root/reference")):
-    if (candidate / "packed_encoders" / "__init__.py").exists() and str(candidate) not in sys.path:
-        sys.path.append(str(candidate))
-        break
+from oracle.reference_tree import add_reference_to_path
 
+add_reference_to_path()
 pe_ref = pytest.importorskip("packed_encoders")
 
 
@@ -55,6 +49,80 @@ def test_backend_resolution_keeps_b200(installed):
 
     workload = attention_dispatch.AttentionWorkload.from_lengths([5, 300, 17])
     assert forward._resolve_eager_backend("b200", workload, triton_supported=True, flash_available=True) == "b200"
+
+
+def _fake_device(monkeypatch, cc, name):
+    from packed_encoders import attention_dispatch
+
+    monkeypatch.setattr(attention_dispatch, "current_compute_capability", lambda: cc)
+    monkeypatch.setattr(attention_dispatch, "current_device_name", lambda: name)
+
+
+def test_default_and_auto_resolve_to_b200_on_sm100(installed, monkeypatch):
+    """The single b200 backend replaces the calibrated Triton-vs-FA policy on sm_100
+    (attention_dispatch.py:129-139 holds the B200 threshold it no longer reaches): the default
+    backend of pe.pack (pack.py:147-158), the "auto" branch of pack._resolve_attention_backend
+    (pack.py:161-192) and of forward._resolve_eager_backend (forward.py:320-331, eager and
+    for_cuda_graph) all give "b200"; the rectangular graph runner is not built for it."""
+    import importlib
+
+    from packed_encoders import attention_dispatch, forward, graph
+
+    pack = importlib.import_module("packed_encoders.pack")  # the package re-exports a function of this name
+    _fake_device(monkeypatch, (10, 0), "NVIDIA B200")
+    consulted = []
+    orig_policy = attention_dispatch.get_packed_inference_policy
+    monkeypatch.setattr(attention_dispatch, "get_packed_inference_policy",
+                        lambda *a, **k: consulted.append(1) or orig_policy(*a, **k))
+    workload = attention_dispatch.AttentionWorkload.from_lengths([5, 300, 17])
+    with torch.no_grad():
+        assert pack._default_backend() == "b200"
+        assert pack._resolve_attention_backend("auto") == "b200"
+        assert pack._resolve_attention_backend("b200") == "b200"
+        for for_graph in (False, True):
+            assert forward._resolve_eager_backend("auto", workload, triton_supported=True, flash_available=True,
+                                                  for_cuda_graph=for_graph) == "b200"
+        # explicit choices are left alone
+        assert forward._resolve_eager_backend("sdpa", workload, triton_supported=True, flash_available=True) == "sdpa"
+        assert forward._resolve_eager_backend("flash", workload, triton_supported=True, flash_available=True) == "flash"
+    assert not consulted
+    assert graph.rectangular_graph_backend("b200") is None
+    # training keeps the reference's resolution (the kernels are forward-only)
+    with torch.enable_grad():
+        assert forward._resolve_eager_backend("auto", workload, triton_supported=True, flash_available=True) == "flash"
+
+
+def test_other_devices_keep_the_reference_policy(installed, monkeypatch):
+    import importlib
+
+    from packed_encoders import attention_dispatch, forward
+
+    pack = importlib.import_module("packed_encoders.pack")
+    _fake_device(monkeypatch, (9, 0), "NVIDIA H200")
+    workload = attention_dispatch.AttentionWorkload.from_lengths([5, 300, 17])
+    with torch.no_grad():
+        assert pack._resolve_attention_backend("auto") != "b200"
+        got = forward._resolve_eager_backend("auto", workload, triton_supported=True, flash_available=True)
+        # the H200 policy keeps Triton below 131,073 live tokens (attention_dispatch.py:124-127)
+        assert got == "triton"
+
+
+def test_pack_without_backend_prepares_b200_on_sm100(installed, monkeypatch):
+    """pe.pack(model) with no attention_backend on an sm_100 device prepares the b200 state; the
+    preparation itself needs no GPU (validation off, the CUDA requirement faked)."""
+    import importlib
+
+    pack = importlib.import_module("packed_encoders.pack")
+    _fake_device(monkeypatch, (10, 0), "NVIDIA B200")
+    monkeypatch.setattr(pack, "_require_cuda", lambda encoder: None)
+    from transformers import ModernBertConfig, ModernBertModel
+
+    cfg = ModernBertConfig(vocab_size=512, hidden_size=128, intermediate_size=192, num_hidden_layers=3,
+                           num_attention_heads=2, local_attention=128, global_attn_every_n_layers=3,
+                           max_position_embeddings=1024, pad_token_id=0)
+    model = ModernBertModel(cfg).eval()
+    state = pack._prepare_modernbert(model, validate=False)
+    assert state.attention_backend == "b200"
 
 
 def test_candidate_forms_call_the_kernels(installed, monkeypatch):

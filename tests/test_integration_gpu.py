@@ -16,18 +16,14 @@ reference's own GPU tests:
 from __future__ import annotations
 
 import copy
-import sys
-from pathlib import Path
 
 import pytest
 import torch
 import torch.nn.functional as F
 
-ROOT = Path(__file__).resolve().parents[1]
-for candidate in (ROOT / "baseline" / "_ref",):
-    if (candidate / "packed_encoders" / "__init__.py").exists() and str(candidate) not in sys.path:
-        sys.path.append(str(candidate))
-        break
+from oracle.reference_tree import add_reference_to_path
+
+add_reference_to_path()
 
 pytestmark = pytest.mark.gpu
 pe_ref = pytest.importorskip("packed_encoders")
@@ -85,6 +81,36 @@ def test_pack_b200_matches_stock_hf_on_padded_batch(b200):
     assert torch.isfinite(out[am.bool()]).all()
     assert _masked_cos(out, ref, am) > 0.997
     assert _per_token_min_cos(out, ref, am) > 0.98
+
+
+def test_pack_with_default_backend_runs_b200_kernels(b200):
+    """pe.pack(model) with no attention_backend on an sm_100 GPU resolves to "b200" (the
+    calibrated Triton-vs-FA policy is replaced, attention_dispatch.py:129-139) and the forward
+    launches this library's kernels; outputs match stock HF."""
+    from packed_encoders_b200 import ops as b200_ops
+
+    if torch.cuda.get_device_capability() != (10, 0):
+        pytest.skip("the b200 default applies to sm_100 devices")
+    stock = _tiny_modernbert(seed=4)
+    packed = copy.deepcopy(stock)
+    pe_ref.pack(packed, validate=False)
+    from packed_encoders.state import ATTR
+
+    assert getattr(packed, ATTR).attention_backend == "b200"
+    lengths = [9, 200, 1, 64]
+    s = max(lengths)
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    ids = torch.randint(1, 512, (len(lengths), s), device="cuda", generator=gen)
+    am = torch.zeros_like(ids)
+    for i, n in enumerate(lengths):
+        am[i, :n] = 1
+    ids = ids * am
+    before = b200_ops.LAUNCHES["kernels"]
+    with torch.inference_mode():
+        out = packed(input_ids=ids, attention_mask=am).last_hidden_state
+        ref = stock(input_ids=ids, attention_mask=am).last_hidden_state
+    assert b200_ops.LAUNCHES["kernels"] > before
+    assert _masked_cos(out, ref, am) > 0.997
 
 
 def test_packed_forward_b200_matches_reference_sdpa_backend(b200):
