@@ -43,38 +43,10 @@ constexpr int kHeaderBytes = 256;         // workspace header: n_items, error wo
 // L2 policies of the TMA copies: Q tiles are read once (evict first); K/V tiles are re-read by
 // every query block of their sequence (0 normal, 1 evict last). Output rows are written with
 // streaming stores.
-#ifndef PE_B200_KV_POLICY
-#define PE_B200_KV_POLICY 0
-#endif
-#ifndef PE_B200_L2_PROMOTION
-#define PE_B200_L2_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_256B
-#endif
 constexpr bool kQEvictFirst = true;
-constexpr int kKVPolicy = PE_B200_KV_POLICY;
+constexpr int kKVPolicy = 0;
 constexpr bool kStreamOut = true;
 
-#ifdef PE_B200_TRACE
-// Phase timing of block 0's warps (experiment builds only): per warp, clock64 sums per phase.
-__device__ unsigned long long g_trace[8][16];
-#define PE_TCLK(v) const long long v = clock64()
-#define PE_TDECL unsigned long long tacc[8] = {0, 0, 0, 0, 0, 0, 0, 0}
-#define PE_TADD(w, ph, a, b) tacc[ph] += (unsigned long long)((b) - (a))
-#define PE_TFLUSH(w)                                                          \
-  if (blockIdx.x == 0 && (threadIdx.x & 31) == 0) {                          \
-    for (int ph_ = 0; ph_ < 8; ++ph_) g_trace[w][ph_] += tacc[ph_];          \
-  }
-// Per-step event times of block 0's first 256 key tiles: [0] QK issued (MMA warp, after the
-// s_full commit), [1] S ready seen by softmax warp 2, [2] P arrival of warp 2, [3] PV issued.
-__device__ long long g_events[4][256];
-#define PE_TEV(kind, step)                                                                   \
-  if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (step) < 256) g_events[kind][step] = clock64()
-#else
-#define PE_TCLK(v)
-#define PE_TDECL
-#define PE_TADD(w, ph, a, b)
-#define PE_TFLUSH(w)
-#define PE_TEV(kind, step)
-#endif
 constexpr int kCostBuckets = 1024;        // LPT ordering buckets (cost clamped)
 constexpr int kBuilderThreads = 1024;
 constexpr float kRescaleThreshold = 8.0f; // log2 units: rescale O only when the max grows > 2^8
@@ -297,18 +269,9 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //        than PASS is re-read from TMEM for the exp pass.
 //   TMA_OUT windowed-layer epilogue through one TMA store per warp; GATE output gate fused into
 //        the epilogue; STAGE epilogue rows staged through shared memory (head_dim 64).
-//   P_SMEM P goes to shared memory (128B-swizzled, K-major) and P.V reads it from there (SS
-//        MMA) instead of from TMEM. An S buffer is then free as soon as the softmax warps have
-//        loaded it into registers, so the next QK does not wait for this tile's P.V, and a CTA
-//        needs only NS*BN + D TMEM columns (three CTAs per SM at head_dim 64 with NS = 1).
 template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_ = 0, int PASS_ = 0,
-          bool TMA_OUT_ = false, bool GATE_ = false, bool STAGE_ = true, bool P_SMEM_ = false, bool P_TMEM_ = false>
+          bool TMA_OUT_ = false, bool GATE_ = false, bool STAGE_ = true>
 struct Cfg {
-  static constexpr bool kPSmem = P_SMEM_;
-  // P_TMEM: P goes to its own TMEM region (BN/2 columns, a second allocation) instead of over S,
-  // with the same early release of S as P_SMEM but no extra shared-memory traffic.
-  static constexpr bool kPTmem = P_TMEM_;
-  static constexpr bool kPSep = P_SMEM_ || P_TMEM_;  // S is released once loaded into registers
   static constexpr bool kGate = GATE_;  // output gate fused into the epilogue (calls with a gate)
   static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_;
   static constexpr int kPass = PASS_ > 0 ? PASS_ : (BN < 64 ? BN : 64);
@@ -325,14 +288,10 @@ struct Cfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + QB * kQBytes;
   static constexpr int kOffV = kOffK + ST * kKVBytes;
-  // P buffer (P_SMEM): 128 rows x BN keys bf16, BN/64 panels of 128 x 128 B; warp w's 32 rows are
-  // the 4 KB at w * 4096 of each panel, which also serve as that warp's epilogue stage.
-  static constexpr int kPBytes = P_SMEM_ ? kTileM * BN * 2 : 0;
-  static constexpr int kOffP = kOffV + VST * kKVBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;
+  static constexpr int kOffBar = kOffV + VST * kKVBytes;
   // barriers: k_full[ST] k_empty[ST] v_full[VST] v_empty[VST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS]
-  //           o_full row_empty[QB] (P_SMEM: s_free[NS] p_free)
-  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1 + (kPSep ? NS + 1 : 0);
+  //           o_full row_empty[QB]
+  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   // Epilogue staging (2 KB per softmax warp) so output rows leave as coalesced 128-byte lines;
   // only where shared memory allows (head_dim 64).
@@ -344,7 +303,7 @@ struct Cfg {
   static constexpr bool kTmaOut = TMA_OUT_ && kStageOut;
   static constexpr int kStageAlign = kTmaOut ? 1024 : 128;  // the 128-byte swizzle needs 1 KB
   static constexpr int kOffStage = (kOffTmemSlot + 16 + kStageAlign - 1) & ~(kStageAlign - 1);
-  static constexpr int kStageBytes = P_SMEM_ ? 0 : kTmaOut ? 4 * 4096 : kStageOut ? 4 * 2048 : 0;
+  static constexpr int kStageBytes = kTmaOut ? 4 * 4096 : kStageOut ? 4 * 2048 : 0;
   // Per Q buffer: the unit's header (UnitInfo fields) and every row's allowed key interval,
   // written by the producer so the softmax warps read no schedule data from global memory.
   static constexpr int kRowSlotBytes = 64 + kTileM * 8;
@@ -357,14 +316,9 @@ struct Cfg {
   // CPS CTAs must fit one SM together: 228 KB of shared memory (1 KB of it reserved per CTA).
   static_assert((kSmemBytes + 1024) * CPS <= 228 * 1024, "shared memory of CPS CTAs per SM");
   static_assert(BN % 64 == 0 && D % 64 == 0 && BN % kPass == 0 && kPass % 32 == 0, "tile shape");
-  static_assert(!kPSep || (BN == 64 && kPass == 64), "P_SMEM / P_TMEM: one 64-key panel per S tile");
-  static_assert(!(P_SMEM_ && P_TMEM_), "one P location");
-  static constexpr uint32_t kTmemColsP = P_TMEM_ ? 32 : 0;  // the P region (BN / 2 columns of bf16 pairs)
-  static_assert((kTmemCols + kTmemColsP) * CPS <= 512, "TMEM shared by the CTAs of one SM");
-  // Epilogue stage of warp w (4 KB, 1 KB aligned): its own rows of the P buffer under P_SMEM.
-  __device__ static constexpr int stage_off(int w) {
-    return P_SMEM_ ? kOffP + w * 4096 : kOffStage + w * (kTmaOut ? 4096 : 2048);
-  }
+  static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
+  // Epilogue stage of warp w (4 KB with TMA_OUT, else 2 KB).
+  __device__ static constexpr int stage_off(int w) { return kOffStage + w * (kTmaOut ? 4096 : 2048); }
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
 };
 
@@ -658,8 +612,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
   uint64_t* p_full = s_full + C::NS;
   uint64_t* o_full = p_full + C::NS;  // the last P.V of each unit (epilogue)
   uint64_t* row_empty = o_full + 1;    // [QB] the softmax warps took the unit's row slot
-  uint64_t* s_free = row_empty + C::QB;  // [NS] (P_SMEM) the softmax warps hold S in registers
-  uint64_t* p_free = s_free + C::NS;     // (P_SMEM) the P.V reading the P buffer has completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -684,15 +636,10 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
     }
     mbar_init(o_full, 1);
     for (int i = 0; i < C::QB; ++i) mbar_init(&row_empty[i], 4);
-    if constexpr (C::kPSep) {
-      for (int i = 0; i < C::NS; ++i) mbar_init(&s_free[i], 4);
-      mbar_init(p_free, 1);
-    }
     fence_mbar_init();
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
-    if constexpr (C::kPTmem) tmem_alloc(tmem_slot + 1, C::kTmemColsP);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
@@ -704,7 +651,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_p = C::kPTmem ? tmem_slot[1] : 0u;  // P region (P_TMEM)
   const long long n_units = (long long)p.header->n_items * p.heads;
 
   if (warp == 0) {
@@ -804,7 +750,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileM, C::BN, false, false);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kTileM, C::D, false, true);
       const uint32_t smem_base = smem_u32(smem);
-      PE_TDECL;
       uint32_t i = 0;
       int lu = 0;
       // P.V runs kLag key tiles behind QK: with a third S buffer the QK two tiles ahead is
@@ -816,11 +761,8 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       auto issue_pv = [&](uint32_t j, int first, int last) {
         const int sb = (int)(j % C::NS);
         const int st = (int)(j % C::VST);
-        PE_TCLK(tm0);
         mbar_wait(&p_full[sb], (int)(j / C::NS) & 1, p.err);
         mbar_wait(&v_full[st], (int)(j / C::VST) & 1, p.err);
-        PE_TCLK(tm1);
-        PE_TADD(1, 0, tm0, tm1);
         tc_fence_after();
         const uint32_t v_addr = smem_base + C::kOffV + st * C::kKVBytes;
 #pragma unroll
@@ -828,28 +770,16 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           uint64_t bdesc[4];
 #pragma unroll
           for (int k4 = 0; k4 < 4; ++k4) bdesc[k4] = sw128_desc(v_addr + (g * 4 + k4) * 16 * 128, C::kKVPanelBytes, 1024);
-          if constexpr (C::kPSmem) {  // P from the shared-memory P buffer (K-major, like Q)
-            uint64_t adesc[4];
+          uint32_t a_tm[4];
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) adesc[k4] = sw128_desc(smem_base + C::kOffP + g * kTileM * 128 + k4 * 32, 16, 1024);
-            mma_ss4_w(tmem + C::kColO, adesc, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
-          } else {
-            uint32_t a_tm[4];
-            const uint32_t p_base = C::kPTmem ? tmem_p : tmem + C::col_s(sb);
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) a_tm[k4] = p_base + (g * 4 + k4) * 8;
-            mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
-          }
+          for (int k4 = 0; k4 < 4; ++k4) a_tm[k4] = tmem + C::col_s(sb) + (g * 4 + k4) * 8;
+          mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
         }
         // One completion per unit (the epilogue waits on it, so it is committed first): with two
         // S buffers the next unit's QK is issued before this P.V, so S-ready no longer implies
         // earlier P.V completions.
         if (last) mma_commit_w(o_full);
-        if constexpr (C::kPSep) mma_commit_w(p_free);
         mma_commit_w(&v_empty[st]);
-        PE_TCLK(tm2);
-        PE_TADD(1, 1, tm1, tm2);
-        PE_TEV(3, j);
       };
       auto flush_one = [&]() {
         issue_pv(pend0, (int)(pfirst & 1u), (int)(plast & 1u));
@@ -874,17 +804,10 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         for (int t = 0; t < n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
           const int sb = (int)(i % C::NS);
-          if constexpr (C::kPSep) {
-            // The S buffer is reused once the softmax warps hold its previous tile in registers.
-            if (i >= C::NS) mbar_wait(&s_free[sb], (int)((i / C::NS) - 1) & 1, p.err);
-          } else if (C::NS == 1) {
-            // With one S buffer the previous P must be consumed first (issue order = execution order).
+          // With one S buffer the previous P must be consumed first (issue order = execution order).
+          if (C::NS == 1)
             while (npend > 0) flush_one();
-          }
-          PE_TCLK(tq0);
           mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
-          PE_TCLK(tq1);
-          PE_TADD(1, 2, tq0, tq1);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
 #pragma unroll
@@ -900,10 +823,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           mma_commit_w(&s_full[sb]);
           mma_commit_w(&k_empty[st]);
           if (t == n_kv - 1) mma_commit_w(&q_empty[qb]);
-          PE_TCLK(tq2);
-          PE_TADD(1, 3, tq1, tq2);
-          PE_TEV(0, i);
-          PE_TADD(1, 5, 0, 1);
           if (npend == 0) pend0 = i;
           pfirst |= (t == 0 ? 1u : 0u) << npend;
           plast |= (t == n_kv - 1 ? 1u : 0u) << npend;
@@ -912,7 +831,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         }
       }
       while (npend > 0) flush_one();
-      PE_TFLUSH(1);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -926,10 +844,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
     const uint32_t o_addr = tmem + lane_base + C::kColO;
     const float NEG_INF = -__int_as_float(0x7f800000);
     const float c2 = p.scale_log2;
-    // P_SMEM: this thread's row of the P buffer (warp `quarter` owns the 4 KB at quarter * 4096).
-    uint8_t* p_row = smem + C::kOffP + (r >> 3) * 1024 + (r & 7) * 128;
-    bool stage_busy = false;  // a TMA store from this warp's stage may still read it
-    PE_TDECL;
     uint32_t i = 0;
     int lu = 0;
     for (;; ++lu) {
@@ -949,12 +863,10 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       const int klo = kr.x, khi = kr.y;
       __syncwarp();
       if (lane == 0) mbar_arrive(&row_empty[qb]);
-      PE_TCLK(tu0);
       const bool row_valid = r < ui.nq;
       const int tq = ui.q_row0 + r;
       float m_run = NEG_INF, l_run = 0.f;
       for (int t = 0; t < ui.n_kv; ++t, ++i) {
-        PE_TCLK(tr0);
         const int sb = (int)(i % C::NS);
         const uint32_t s_addr = tmem + lane_base + C::col_s(sb);
         const int kt = ui.kv_lo + t * C::BN;
@@ -968,9 +880,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         uint32_t raw[kPass];
         if (kEarlyLd) {
           mbar_wait(&s_full[sb], (int)(i / C::NS) & 1, p.err);
-          PE_TCLK(tr1);
-          PE_TADD(warp, 0, tr0, tr1);
-          if (warp == 2) PE_TEV(1, i);
           tc_fence_after();
 #pragma unroll
           for (int cc = 0; cc < kPass / 32; ++cc)
@@ -998,11 +907,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
                 tmem_ld32(s_addr + h * kPass + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[cc * 32]));
           }
           tmem_wait_ld();
-          if constexpr (C::kPSep) {  // S is in registers: the MMA warp may overwrite the buffer
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[sb]);
-          }
           if (full) {
 #pragma unroll
             for (int j = 0; j + 1 < kPass; j += 2)
@@ -1022,8 +926,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           }
         }
         const float mx = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
-        PE_TCLK(tr3);
-        PE_TADD(warp, 2, tr0, tr3);
         const float m_new = fmaxf(m_run, mx * c2);
         const bool need = (m_run != NEG_INF) && (m_new > m_run + kRescaleThreshold);
         const bool any_need = __any_sync(0xffffffffu, need);
@@ -1071,32 +973,9 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
 #pragma unroll
               for (int j = 0; j < 16; ++j) pk[j] = 0u;
             }
-            if constexpr (C::kPSmem) {
-              if (cc == 0) {
-                // The P buffer is free once the previous tile's P.V has completed; a TMA store of
-                // this warp's last epilogue may still be reading these rows.
-                if (i > 0) mbar_wait(p_free, (int)((i - 1) & 1), p.err);
-                if (C::kTmaOut && stage_busy) {
-                  if (lane == 0) bulk_wait_read_all();
-                  __syncwarp();
-                  stage_busy = false;
-                }
-              }
-              // Row r, 16-byte chunk c of the 128B-swizzled K-major tile: r*128 + (c ^ r%8)*16.
-#pragma unroll
-              for (int c = 0; c < 4; ++c)
-                *reinterpret_cast<uint4*>(p_row + (((cc * 4 + c) ^ (r & 7)) << 4)) =
-                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-            } else if constexpr (C::kPTmem) {
-              if (cc == 0 && i > 0) mbar_wait(p_free, (int)((i - 1) & 1), p.err);  // the previous P.V is done
-              tmem_st16(tmem_p + lane_base + (h * kPass + cc * 32) / 2, pk);
-            } else {
-              tmem_st16(s_addr + (h * kPass + cc * 32) / 2, pk);
-            }
+            tmem_st16(s_addr + (h * kPass + cc * 32) / 2, pk);
           }
         }
-        PE_TCLK(tr4);
-        PE_TADD(warp, 3, tr3, tr4);
         // O rescale (rare: the running max grew by more than 2^8) after P is out, so the S
         // registers are free and the previous P.V has had the softmax time to finish.
         if (any_need) {
@@ -1121,18 +1000,12 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         }
         const float2 acc = fadd2(fadd2(accs[0], accs[1]), fadd2(accs[2], accs[3]));
         l_run += acc.x + acc.y;
-        if constexpr (C::kPSmem) fence_proxy_async_smem();  // P stores visible to the tensor core
-        if (!C::kPSmem || any_need) tmem_wait_st();
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[sb]);
-        PE_TCLK(tr5);
-        PE_TADD(warp, 4, tr4, tr5);
-        if (warp == 2) PE_TEV(2, i);
-        PE_TADD(warp, 5, 0, 1);  // steps
       }
       // Epilogue: O / l -> bf16 rows, LSE in natural log.
-      PE_TCLK(tu1);
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       // Gated calls (rows stored by their own thread): the first gate chunk is in flight while
       // the last P.V completes.
@@ -1182,7 +1055,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           else tma_store_3d(&tm_o, stage, 0, ui.head, ui.q_row0 + quarter * 32);
           bulk_commit_group();
         }
-        stage_busy = true;
       } else if constexpr (C::kStageOut) {
         // 64 output columns per thread, in two 32-column halves: each half of all 32 rows of the
         // warp goes through a 2 KB buffer (16-byte chunk c of row r at r*4 + (c ^ (r/2 % 4)),
@@ -1256,12 +1128,8 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         const float lse = l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : NEG_INF;
         p.lse[(long long)ui.head * p.total_q + tq] = lse;
       }
-      PE_TCLK(tu2);
-      PE_TADD(warp, 6, tu0, tu2);
-      PE_TADD(warp, 7, tu1, tu2);
       tc_fence_before();
     }
-    PE_TFLUSH(warp);
     if (C::kTmaOut && lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
 
@@ -1270,7 +1138,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
-    if constexpr (C::kPTmem) tmem_dealloc(tmem_p, C::kTmemColsP);
   }
 }
 
@@ -1441,7 +1308,7 @@ static bool make_map(CUtensorMap* map, const void* base, long long tokens, int h
   cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, PE_B200_L2_PROMOTION,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -1459,7 +1326,7 @@ static bool make_map_panels(CUtensorMap* map, const void* base, long long tokens
   cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, (cuuint32_t)(dim / 64)};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, PE_B200_L2_PROMOTION,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -1510,18 +1377,6 @@ static bool gate_as_own_pass() {
   }();
   return own_pass;
 }
-
-#ifdef PE_B200_EXPERIMENTS
-// Layout experiments (built only with -DPE_B200_EXPERIMENTS; the shipped library has none):
-// PE_B200_EXP selects a head_dim-64 configuration, read once per process.
-static int experiment() {
-  static const int e = [] {
-    const char* v = getenv("PE_B200_EXP");
-    return (v && *v) ? atoi(v) : 0;
-  }();
-  return e;
-}
-#endif
 
 static long long item_capacity(const PeB200AttnParams* p) {
   return (long long)p->n_seq + (long long)p->total_q / kTileM + 2;
@@ -1747,27 +1602,6 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   switch (p->head_dim) {
     case 64: {
       const bool windowed = (p->window_left >= 0 || p->window_right >= 0) && !p->causal;
-#ifdef PE_B200_EXPERIMENTS
-      switch (experiment()) {
-        case 1: return launch_attention<Cfg<64, 64, 2, 2, 1, 1, 4, 0, 32, false, false, false>>(p, s, info.sms);
-        case 2: return launch_attention<Cfg<64, 64, 2, 2, 1, 1, 4, 0, 64, false, false, false>>(p, s, info.sms);
-        case 3: return launch_attention<Cfg<64, 64, 3, 3, 1, 1, 3, 0, 32, false, false, false>>(p, s, info.sms);
-        case 4: return launch_attention<Cfg<64, 64, 3, 3, 1, 1, 3, 0, 64, false, false, false>>(p, s, info.sms);
-        case 5: return launch_attention<Cfg<64, 64, 3, 2, 1, 1, 3, 0, 64>>(p, s, info.sms);
-        case 10: return launch_attention<Cfg<64, 64, 2, 2, 2, 1, 3, 0, 0, false, false, false, false, true>>(p, s, info.sms);
-        case 11: return launch_attention<Cfg<64, 64, 3, 2, 1, 1, 3, 0, 0, false, false, true, false, true>>(p, s, info.sms);
-        case 12: return launch_attention<Cfg<64, 64, 2, 2, 1, 1, 3, 0, 0, false, false, true, false, true>>(p, s, info.sms);
-        case 13: return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2>>(p, s, info.sms);
-        case 14: return launch_attention<Cfg<64, 64, 4, 4, 2, 3, 2>>(p, s, info.sms);
-        case 15: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 4>>(p, s, info.sms);
-        case 16: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 2>>(p, s, info.sms);
-        case 17: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 6>>(p, s, info.sms);
-        case 18: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 3>>(p, s, info.sms);
-        case 19: return launch_attention<Cfg<64, 64, 4, 3, 2, 1, 2, 0, 0, false, false, true, false, true>>(p, s, info.sms);
-        case 20: return launch_attention<Cfg<64, 64, 4, 3, 2, 1, 2, 4, 0, false, false, true, false, true>>(p, s, info.sms);
-        default: break;
-      }
-#endif
       // 64-key tiles, two CTAs per SM. Windowed layers: three S buffers and the TMA-store
       // epilogue. Batches of short sequences (query batches: units of one or two key tiles) also
       // run P.V two tiles behind QK (config 2 -2.3 %); long global sequences measured +1.4 % so.
@@ -1781,21 +1615,6 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
     default: return PE_B200_ERR_UNSUPPORTED;
   }
 }
-
-#ifdef PE_B200_TRACE
-int pe_b200_trace_events(long long* out) {
-  return cudaMemcpyFromSymbol(out, g_events, sizeof(g_events)) == cudaSuccess ? PE_B200_OK : PE_B200_ERR_CUDA;
-}
-
-int pe_b200_trace_read(unsigned long long* out, int clear) {
-  if (cudaMemcpyFromSymbol(out, g_trace, sizeof(g_trace)) != cudaSuccess) return PE_B200_ERR_CUDA;
-  if (clear) {
-    static const unsigned long long zero[8][16] = {};
-    cudaMemcpyToSymbol(g_trace, zero, sizeof(zero));
-  }
-  return PE_B200_OK;
-}
-#endif
 
 int pe_b200_attn_fwd(const PeB200AttnParams* p, void* stream) {
   int st = validate(p, kFull);
