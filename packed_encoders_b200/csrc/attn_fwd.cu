@@ -96,6 +96,7 @@ struct AttnParams {
   const __nv_bfloat16* gate;  // optional output gate [total_q, heads, D]
   long long g_tok;
   long long g_head;
+  int kv_major;  // unit order (unit_coords)
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -431,33 +432,6 @@ struct UnitInfo {
   int kv_lo, n_kv;
 };
 
-template <int BN>
-__device__ __forceinline__ UnitInfo unit_info_from(const AttnParams& p, const WorkItem& it, long long u) {
-  UnitInfo ui;
-  ui.head = (int)(u % p.heads);
-  ui.kv_head = ui.head / p.group;
-  ui.f = it.seq_first;
-  ui.c = it.seq_count;
-  ui.qb = it.q_block;
-  const int cq0 = p.cu_q[ui.f], cqe = p.cu_q[ui.f + ui.c];
-  ui.q_row0 = cq0 + ui.qb * kTileM;
-  ui.nq = min(kTileM, cqe - ui.q_row0);
-  int kv_lo, kv_hi;
-  if (ui.c == 1) {
-    const int ck0 = p.cu_k[ui.f];
-    int lo, hi;
-    block_key_range(ui.qb, ui.nq, cqe - cq0, p.cu_k[ui.f + 1] - ck0, p.window_left, p.window_right, lo, hi);
-    kv_lo = ck0 + lo;
-    kv_hi = ck0 + hi;
-  } else {
-    kv_lo = p.cu_k[ui.f];
-    kv_hi = p.cu_k[ui.f + ui.c];
-  }
-  ui.kv_lo = kv_lo;
-  ui.n_kv = (ui.nq > 0 && kv_hi > kv_lo) ? (kv_hi - kv_lo + BN - 1) / BN : 0;
-  return ui;
-}
-
 // Segment bounds a unit needs: cu_q[f], cu_q[f + c], cu_k[f], cu_k[f + c] (for one sequence,
 // c = 1, the last two are its key segment).
 __device__ __forceinline__ int4 unit_bounds(const AttnParams& p, const WorkItem& it) {
@@ -465,11 +439,32 @@ __device__ __forceinline__ int4 unit_bounds(const AttnParams& p, const WorkItem&
                    p.cu_k[it.seq_first + it.seq_count]);
 }
 
-// UnitInfo of unit u from its schedule entry and bounds (arithmetic only; as unit_info).
+// Unit order. Item-major (units u = item * heads + head): the heads of a query block run
+// together, so the 256-byte L2 lines of a token's K/V rows (two heads each) are used at once; best
+// for windowed layers and batches of short sequences. KV-major (kv_major: KV head, then item, then
+// the query heads sharing that KV head): the ~296 units resident at a time cover many query
+// blocks of one (sequence, KV head) instead of a few blocks of every head, so the K/V of a long
+// sequence is read from DRAM about once and served from L2 to all its query blocks (item-major
+// order re-reads it for every wave of resident units the sequence spans).
+__device__ __forceinline__ void unit_coords(uint32_t u, uint32_t n_items, uint32_t group, uint32_t heads,
+                                            bool kv_major, uint32_t& item, int& head) {
+  if (!kv_major) {
+    item = u / heads;
+    head = (int)(u - item * heads);
+    return;
+  }
+  const uint32_t per_kv = n_items * group;
+  const uint32_t kvh = u / per_kv;
+  const uint32_t rem = u - kvh * per_kv;
+  item = rem / group;
+  head = (int)(kvh * group + (rem - item * group));
+}
+
+// UnitInfo of a unit from its schedule entry, bounds and head (arithmetic only).
 template <int BN>
-__device__ __forceinline__ UnitInfo unit_derive(const AttnParams& p, const WorkItem& it, int4 b, uint32_t u) {
+__device__ __forceinline__ UnitInfo unit_derive(const AttnParams& p, const WorkItem& it, int4 b, int head) {
   UnitInfo ui;
-  ui.head = (int)(u % (uint32_t)p.heads);
+  ui.head = head;
   ui.kv_head = ui.head / p.group;
   ui.f = it.seq_first;
   ui.c = it.seq_count;
@@ -491,53 +486,54 @@ __device__ __forceinline__ UnitInfo unit_derive(const AttnParams& p, const WorkI
   return ui;
 }
 
-template <int BN>
-__device__ __forceinline__ UnitInfo unit_info(const AttnParams& p, long long u) {
-  const WorkItem it = p.items[u / p.heads];
-  return unit_derive<BN>(p, it, unit_bounds(p, it), (uint32_t)u);
-}
-
 // The CTA's units (b, b + grid, ...) for the producer, as a three-stage pipeline so that moving
 // to the next unit waits on no global load: the schedule entry of the unit three ahead and the
 // segment bounds of the unit two ahead are loaded one advance before they are used, and the next
 // unit's UnitInfo is then arithmetic only.
 template <int BN>
 struct UnitStream {
-  uint32_t u, n, step;
+  uint32_t u, n, step, n_items, group, heads;
+  bool kv_major;
   UnitInfo cur, nxt;
   WorkItem it2, it3;  // schedule entries of units u + 2*step, u + 3*step
   int4 b2;            // bounds of unit u + 2*step
-  __device__ __forceinline__ WorkItem item(const AttnParams& p, uint32_t v) const {
-    return p.items[v / (uint32_t)p.heads];
+  int h2, h3;         // heads of units u + 2*step, u + 3*step
+  __device__ __forceinline__ WorkItem item(const AttnParams& p, uint32_t v, int& head) const {
+    uint32_t idx;
+    unit_coords(v, n_items, group, heads, kv_major, idx, head);
+    return p.items[idx];
   }
-  __device__ __forceinline__ UnitStream(const AttnParams& p, long long first, long long n_units, long long stride)
-      : u((uint32_t)first), n((uint32_t)n_units), step((uint32_t)stride) {
+  __device__ __forceinline__ UnitStream(const AttnParams& p, uint32_t items, uint32_t first, uint32_t stride)
+      : u(first), n(items * (uint32_t)p.heads), step(stride), n_items(items), group((uint32_t)p.group),
+        heads((uint32_t)p.heads), kv_major(p.kv_major != 0) {
     cur.n_kv = 0;
     nxt.n_kv = 0;
+    int h;
     if (u < n) {
-      const WorkItem it = item(p, u);
-      cur = unit_derive<BN>(p, it, unit_bounds(p, it), u);
+      const WorkItem it = item(p, u, h);
+      cur = unit_derive<BN>(p, it, unit_bounds(p, it), h);
     }
     if (u + step < n) {
-      const WorkItem it = item(p, u + step);
-      nxt = unit_derive<BN>(p, it, unit_bounds(p, it), u + step);
+      const WorkItem it = item(p, u + step, h);
+      nxt = unit_derive<BN>(p, it, unit_bounds(p, it), h);
     }
     if (u + 2 * step < n) {
-      it2 = item(p, u + 2 * step);
+      it2 = item(p, u + 2 * step, h2);
       b2 = unit_bounds(p, it2);
     }
-    if (u + 3 * step < n) it3 = item(p, u + 3 * step);
+    if (u + 3 * step < n) it3 = item(p, u + 3 * step, h3);
   }
   __device__ __forceinline__ bool valid() const { return u < n; }
   __device__ __forceinline__ void advance(const AttnParams& p) {
     u += step;
     cur = nxt;
-    if (u + step < n) nxt = unit_derive<BN>(p, it2, b2, u + step);
+    if (u + step < n) nxt = unit_derive<BN>(p, it2, b2, h2);
     if (u + 2 * step < n) {
       it2 = it3;
+      h2 = h3;
       b2 = unit_bounds(p, it2);
     }
-    if (u + 3 * step < n) it3 = item(p, u + 3 * step);
+    if (u + 3 * step < n) it3 = item(p, u + 3 * step, h3);
   }
 };
 
@@ -651,7 +647,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const long long n_units = (long long)p.header->n_items * p.heads;
+  const uint32_t n_items = (uint32_t)p.header->n_items;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -688,7 +684,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           load_kv(vs, &tm_v, 0, kvh, row, &v_full[st]);
         }
       };
-      for (UnitStream<C::BN> us(p, blockIdx.x, n_units, gridDim.x); us.valid(); us.advance(p)) {
+      for (UnitStream<C::BN> us(p, n_items, blockIdx.x, gridDim.x); us.valid(); us.advance(p)) {
         const UnitInfo ui = us.cur;
         if (ui.n_kv == 0) continue;
         const int qb = lu % C::QB;
@@ -1300,7 +1296,8 @@ static int launch_status(const char* where) {
 }
 
 static bool make_map(CUtensorMap* map, const void* base, long long tokens, int heads, int dim, long long tok_stride,
-                     long long head_stride, int box_rows) {
+                     long long head_stride, int box_rows,
+                     CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)dim, (cuuint64_t)heads, (cuuint64_t)tokens};
@@ -1308,8 +1305,7 @@ static bool make_map(CUtensorMap* map, const void* base, long long tokens, int h
   cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1317,8 +1313,9 @@ static bool make_map(CUtensorMap* map, const void* base, long long tokens, int h
 // bytes) so one copy brings every 64-column panel of a row block, landing panel-major
 // ([panel][row][128 B]) as the MMA descriptors expect.
 static bool make_map_panels(CUtensorMap* map, const void* base, long long tokens, int heads, int dim,
-                            long long tok_stride, long long head_stride, int box_rows) {
-  if (dim <= 64) return make_map(map, base, tokens, heads, dim, tok_stride, head_stride, box_rows);
+                            long long tok_stride, long long head_stride, int box_rows,
+                            CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B) {
+  if (dim <= 64) return make_map(map, base, tokens, heads, dim, tok_stride, head_stride, box_rows, promo);
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[4] = {64, (cuuint64_t)tokens, (cuuint64_t)heads, (cuuint64_t)(dim / 64)};
@@ -1326,8 +1323,7 @@ static bool make_map_panels(CUtensorMap* map, const void* base, long long tokens
   cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, (cuuint32_t)(dim / 64)};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1436,12 +1432,29 @@ static int validate(const PeB200AttnParams* p, int level) {
   return PE_B200_OK;
 }
 
+// KV-major unit order (unit_coords) for unwindowed calls whose longest query segment spans more
+// than one wave of resident units (its blocks x heads exceed the grid): then item-major order
+// would re-read that sequence's K/V from DRAM for every wave. In that order the K/V maps promote
+// L2 fills to 128 bytes (one head's row) instead of 256 (two heads' rows, the second of which
+// item-major order uses at once and KV-major order does not). One full-size config 3 global
+// launch: DRAM reads 7.39 GB (item-major, 256 B) -> 5.06 GB (KV-major, 256 B) -> 3.65 GB
+// (KV-major, 128 B), against 2.77 GB of algorithmic reads.
+static bool use_kv_major(const PeB200AttnParams* p, int sms, int cps) {
+  const bool windowed = p->window_left >= 0 || (p->window_right >= 0 && !p->causal);
+  const long long blocks = ((long long)p->max_seqlen_q + kTileM - 1) / kTileM;
+  return !windowed && blocks * p->heads > (long long)sms * cps;
+}
+
 template <class C>
 static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int sms) {
   CUtensorMap tq, tk, tv, to;
+  const bool kv_major = use_kv_major(p, sms, C::CPS);
+  const CUtensorMapL2promotion kv_promo = kv_major ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
   if (!make_map_panels(&tq, p->q, p->total_q, p->heads, C::D, p->q_stride_token, p->q_stride_head, kTileM) ||
-      !make_map_panels(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN) ||
-      !make_map_panels(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN) ||
+      !make_map_panels(&tk, p->k, p->total_k, p->kv_heads, C::D, p->k_stride_token, p->k_stride_head, C::BN,
+                       kv_promo) ||
+      !make_map_panels(&tv, p->v, p->total_k, p->kv_heads, C::D, p->v_stride_token, p->v_stride_head, C::BN,
+                       kv_promo) ||
       !make_map(&to, p->out, p->total_q, p->heads, C::D, p->o_stride_token, p->o_stride_head, 32))
     return cuda_fail("tensor map encoding", cudaErrorInvalidValue);
   {  // the dynamic shared-memory opt-in, once per (configuration, device), under a lock
@@ -1476,6 +1489,7 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   ap.gate = static_cast<const __nv_bfloat16*>(p->gate);
   ap.g_tok = p->g_stride_token;
   ap.g_head = p->g_stride_head;
+  ap.kv_major = kv_major ? 1 : 0;
   const long long units = item_capacity(p) * p->heads;
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
