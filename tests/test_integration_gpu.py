@@ -186,3 +186,53 @@ def test_apply_rope_bshd_matches_reference_kernel(b200):
         assert (a.float() - b.float()).abs().max().item() <= 2.0 ** -6 * b.float().abs().max().item()
         assert (a != b).float().mean().item() < 0.01
 
+
+
+@pytest.mark.parametrize("gated", [False, True])
+def test_qwen35_attention_caller_runs_b200(b200, gated):
+    """The Qwen3.5 engine's attention path (arch/qwen3_5/engine.py:551-571 -> execution.py:24-27):
+    OrdinaryExecution.attention calls the engine's bound attention_packed piece with the
+    runtime choice, here the b200 candidate selected for the 8/2/256 causal geometry, and the
+    gated layers apply the engine's sigmoid_gate piece after it. Checked against the oracle (plus
+    the reference's gate roundings) and, for the gated form, against this library's own gate
+    in the attention call (same bits)."""
+    from types import SimpleNamespace
+
+    import oracle
+    from conftest import packed_inputs
+    from packed_encoders.arch.qwen3_5.execution import OrdinaryExecution
+    from packed_encoders.arch.qwen3_5.pieces import default_pieces
+    from packed_encoders.runtime.attention import select_attention
+
+    import packed_encoders_b200 as pe
+
+    choice = select_attention(n_heads=8, n_kv_heads=2, head_dim=256, causal=True, device=torch.device("cuda"),
+                              order=("b200",))
+    assert choice.name == "b200", choice.rejected
+    engine = SimpleNamespace(ops=default_pieces().bind(), attention=choice, causal=True)
+    lengths = [300, 5, 1000, 64, 129]
+    q, k, v, cu = packed_inputs(lengths, 8, 256, kv_heads=2, seed=61)
+    lay = SimpleNamespace(static=None, cu32=cu.cuda(), max_len=max(lengths), lengths=lengths)
+    before = pe.ops.LAUNCHES["kernels"]
+    with torch.inference_mode():
+        o = OrdinaryExecution.attention(engine, q.cuda(), k.cuda(), v.cuda(), lay)
+    torch.cuda.synchronize()
+    assert pe.ops.LAUNCHES["kernels"] > before
+    ref, _ = oracle.attention(q, k, v, cu, scale=256 ** -0.5, causal=True)
+    err = (o.float().cpu() - ref).abs().max().item()
+    print(f"PARITY qwen35 caller: max_abs={err:.5f}")
+    assert err <= 2e-2
+    if gated:
+        gate = (torch.randn(q.shape, generator=torch.Generator().manual_seed(62)) * 2).to(torch.bfloat16).cuda()
+        with torch.inference_mode():
+            y = engine.ops.sigmoid_gate(o.view(o.shape[0], 8, 256), gate)
+            fused = pe.packed_attention(q.cuda(), k.cuda(), v.cuda(), cu.cuda(), max(lengths), scale=256 ** -0.5,
+                                        causal=True, gate=gate)
+        torch.cuda.synchronize()
+        ref_y = (ref.to(torch.bfloat16).float() * torch.sigmoid(gate.float().cpu()).to(torch.bfloat16).float())
+        gerr = (y.float().cpu().view_as(ref_y) - ref_y).abs().max().item()
+        print(f"PARITY qwen35 gated caller: max_abs={gerr:.5f}")
+        assert gerr <= 2e-2
+        # same roundings; a sigmoid within an ulp of a bf16 rounding boundary may round the other way
+        diff = (fused.view(fused.shape[0], -1).float() - y.float()).abs()
+        assert (diff > 0).float().mean().item() < 0.01 and diff.max().item() <= 2e-2
