@@ -18,7 +18,7 @@
 extern "C" {
 #endif
 
-#define PE_B200_ABI_VERSION 4
+#define PE_B200_ABI_VERSION 3
 
 enum {
   PE_B200_OK = 0,
@@ -72,13 +72,6 @@ enum {
  *   copies, in place of the reference's apply_rope_bshd pass (packed_encoders/forward.py:199-205).
  *   head_dim 64 and self-attention only (cu_seqlens_k == cu_seqlens_q, total_k == total_q);
  *   other calls with tables return PE_B200_ERR_UNSUPPORTED.
- * rope_positions (ABI 4): 0 = the tables above have one row per token (rope_rows ignored);
- *   1 = the tables are POSITION tables [rope_rows, head_dim] (the reference's rope_tables(max_seqlen)
- *   before its per-token gather, packed_encoders/forward.py:493-510): token t of segment s uses row
- *   t - cu_seqlens_q[s] (its position inside its sequence, the position_ids convention of
- *   packed_forward, forward.py:455-457), clamped to rope_rows - 1. Then the rotation happens inside
- *   the attention kernel on the landed Q and K tiles (same rule and roundings), nothing rotated
- *   goes through device memory, and the workspace needs no room for rotated copies.
  *
  * Replaces (packed-encoders 0.3.0):
  *   packed_short_attention()      packed_encoders/_kernels/triton_packed_attention.py:175-236
@@ -118,8 +111,6 @@ typedef struct PeB200AttnParams {
   const void* rope_cos; /* ABI 3: optional rotary tables, see above */
   const void* rope_sin;
   int64_t rope_stride_token;
-  int32_t rope_positions; /* ABI 4: 1 = position tables rotated inside the attention kernel */
-  int32_t rope_rows;      /* ABI 4: rows of the position tables */
 } PeB200AttnParams;
 
 /* ABI version of the loaded library (PE_B200_ABI_VERSION). */

@@ -13,7 +13,7 @@ from pathlib import Path
 from packed_encoders_b200.errors import PackedEncodersError
 
 LIB_PATH = Path(__file__).resolve().parent / "libpe_b200.so"
-ABI_VERSION = 4
+ABI_VERSION = 3
 
 _p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -38,7 +38,6 @@ class PeB200AttnParams(ctypes.Structure):
         ("workspace", _p), ("workspace_bytes", ctypes.c_size_t),
         ("gate", _p), ("g_stride_token", _i64), ("g_stride_head", _i64),
         ("rope_cos", _p), ("rope_sin", _p), ("rope_stride_token", _i64),
-        ("rope_positions", _i32), ("rope_rows", _i32),
     ]
 
 

@@ -97,10 +97,6 @@ struct AttnParams {
   long long g_tok;
   long long g_head;
   int kv_major;  // unit order (unit_coords)
-  const __nv_bfloat16* rope_cos;  // position tables [rope_rows, 64] (in-kernel RoPE)
-  const __nv_bfloat16* rope_sin;
-  long long rope_stride;
-  int rope_rows;
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -273,17 +269,14 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //   PASS S columns a softmax thread holds in registers at once (0: min(BN, 64)); a row wider
 //        than PASS is re-read from TMEM for the exp pass.
 //   TMA_OUT windowed-layer epilogue through one TMA store per warp; GATE output gate fused into
-//        the epilogue; STAGE epilogue rows staged through shared memory (head_dim 64);
-//   ROPE rotary embedding inside the kernel: a seventh warp rotates every landed Q and K tile in
-//        shared memory with position tables before the MMA warp reads it (head_dim 64).
+//        the epilogue; STAGE epilogue rows staged through shared memory (head_dim 64).
 template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_ = 0, int PASS_ = 0,
-          bool TMA_OUT_ = false, bool GATE_ = false, bool STAGE_ = true, bool ROPE_ = false>
+          bool TMA_OUT_ = false, bool GATE_ = false, bool STAGE_ = true>
 struct Cfg {
-  static constexpr bool kRope = ROPE_;
   static constexpr bool kGate = GATE_;  // output gate fused into the epilogue (calls with a gate)
   static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_;
   static constexpr int kPass = PASS_ > 0 ? PASS_ : (BN < 64 ? BN : 64);
-  static constexpr int kThreads = ROPE_ ? 224 : 192;
+  static constexpr int kThreads = 192;
   // Registers per thread that let CPS CTAs share an SM's 64K (allocated in steps of 8).
   static constexpr int kMaxRegs = (65536 / (kThreads * CPS)) / 8 * 8 > 255 ? 255 : (65536 / (kThreads * CPS)) / 8 * 8;
   static constexpr int kPanels = D / 64;                 // 64-element (128-byte) column panels
@@ -298,8 +291,8 @@ struct Cfg {
   static constexpr int kOffV = kOffK + ST * kKVBytes;
   static constexpr int kOffBar = kOffV + VST * kKVBytes;
   // barriers: k_full[ST] k_empty[ST] v_full[VST] v_empty[VST] q_full[QB] q_empty[QB] s_full[NS] p_full[NS]
-  //           o_full row_empty[QB] (ROPE: q_rot[QB] k_rot[ST])
-  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1 + (ROPE_ ? QB + ST : 0);
+  //           o_full row_empty[QB]
+  static constexpr int kNumBars = 2 * ST + 2 * VST + 3 * QB + 2 * NS + 1;
   static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
   // Epilogue staging (2 KB per softmax warp) so output rows leave as coalesced 128-byte lines;
   // only where shared memory allows (head_dim 64).
@@ -313,9 +306,8 @@ struct Cfg {
   static constexpr int kOffStage = (kOffTmemSlot + 16 + kStageAlign - 1) & ~(kStageAlign - 1);
   static constexpr int kStageBytes = kTmaOut ? 4 * 4096 : kStageOut ? 4 * 2048 : 0;
   // Per Q buffer: the unit's header (UnitInfo fields) and every row's allowed key interval,
-  // written by the producer so the softmax warps read no schedule data from global memory; with
-  // ROPE also every row's sequence start (its position = token - start).
-  static constexpr int kRowSlotBytes = 64 + kTileM * 8 + (ROPE_ ? kTileM * 4 : 0);
+  // written by the producer so the softmax warps read no schedule data from global memory.
+  static constexpr int kRowSlotBytes = 64 + kTileM * 8;
   static constexpr int kOffRows = kOffStage + kStageBytes;
   static constexpr int kSmemBytes = kOffRows + QB * kRowSlotBytes + 1024;  // + align slack
   static constexpr uint32_t kColO = NS * BN;
@@ -326,7 +318,6 @@ struct Cfg {
   static_assert((kSmemBytes + 1024) * CPS <= 228 * 1024, "shared memory of CPS CTAs per SM");
   static_assert(BN % 64 == 0 && D % 64 == 0 && BN % kPass == 0 && kPass % 32 == 0, "tile shape");
   static_assert(kTmemCols * CPS <= 512, "TMEM shared by the CTAs of one SM");
-  static_assert(!ROPE_ || (D == 64 && BN == 64), "in-kernel RoPE: head_dim 64, 64-key tiles");
   // Epilogue stage of warp w (4 KB with TMA_OUT, else 2 KB).
   __device__ static constexpr int stage_off(int w) { return kOffStage + w * (kTmaOut ? 4096 : 2048); }
   __device__ static constexpr uint32_t col_s(int b) { return (uint32_t)(b * BN); }
@@ -394,28 +385,6 @@ __global__ void __launch_bounds__(256) gate_pass_kernel(__nv_bfloat16* out, cons
 // A token's table row is shared by its heads (L1). Per element pair, in fp32 rounded to bf16
 // (packed_encoders/_kernels/rope.py:5-6, 140-200; the reference CPU path cpu/attention.py:298-301):
 //   y[d] = x[d]*cos[d] - x[d+32]*sin[d],  y[d+32] = x[d+32]*cos[d+32] + x[d]*sin[d+32].
-// Rotate-half RoPE of 16 elements of one head row: xl = dims 8c..8c+7, xh = dims 8c+32..8c+39, with
-// the matching table chunks; fp32 arithmetic rounded to bf16 (packed_encoders/_kernels/rope.py:
-// 5-6, 140-200): y[d] = x[d]*cos[d] - x[d+32]*sin[d], y[d+32] = x[d+32]*cos[d+32] + x[d]*sin[d+32].
-// One function for the pass and for the attention kernel's rotation, so both give the same bits.
-__device__ __forceinline__ void rope16(const uint4 xl, const uint4 xh, const uint4 cl, const uint4 ch, const uint4 sl,
-                                       const uint4 sh, uint4& yl, uint4& yh) {
-  auto e0 = [](uint32_t v) { return __uint_as_float(v << 16); };
-  auto e1 = [](uint32_t v) { return __uint_as_float(v & 0xffff0000u); };
-  const uint32_t lo[4] = {xl.x, xl.y, xl.z, xl.w}, hi[4] = {xh.x, xh.y, xh.z, xh.w};
-  const uint32_t cl4[4] = {cl.x, cl.y, cl.z, cl.w}, ch4[4] = {ch.x, ch.y, ch.z, ch.w};
-  const uint32_t sl4[4] = {sl.x, sl.y, sl.z, sl.w}, sh4[4] = {sh.x, sh.y, sh.z, sh.w};
-  uint32_t ylo[4], yhi[4];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const float a0 = e0(lo[w]), a1 = e1(lo[w]), b0 = e0(hi[w]), b1 = e1(hi[w]);
-    ylo[w] = pack_bf16x2(a0 * e0(cl4[w]) - b0 * e0(sl4[w]), a1 * e1(cl4[w]) - b1 * e1(sl4[w]));
-    yhi[w] = pack_bf16x2(b0 * e0(ch4[w]) + a0 * e0(sh4[w]), b1 * e1(ch4[w]) + a1 * e1(sh4[w]));
-  }
-  yl = make_uint4(ylo[0], ylo[1], ylo[2], ylo[3]);
-  yh = make_uint4(yhi[0], yhi[1], yhi[2], yhi[3]);
-}
-
 __global__ void __launch_bounds__(256) rope_pass_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k,
                                                         long long q_tok, long long q_head, long long k_tok,
                                                         long long k_head, const __nv_bfloat16* cos_t,
@@ -424,6 +393,8 @@ __global__ void __launch_bounds__(256) rope_pass_kernel(const __nv_bfloat16* q, 
                                                         __nv_bfloat16* k_out) {
   const int per_tok = 4 * (heads + kv_heads);
   const long long n = (long long)total * per_tok;
+  auto e0 = [](uint32_t v) { return __uint_as_float(v << 16); };
+  auto e1 = [](uint32_t v) { return __uint_as_float(v & 0xffff0000u); };
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     {
       const int tok = (int)(i / per_tok), t = (int)(i - (long long)tok * per_tok);
@@ -438,10 +409,18 @@ __global__ void __launch_bounds__(256) rope_pass_kernel(const __nv_bfloat16* q, 
       const uint4* s4 = reinterpret_cast<const uint4*>(sin_t + (long long)trow * t_tok);
       const uint4 xl = __ldg(reinterpret_cast<const uint4*>(src) + c), xh = __ldg(reinterpret_cast<const uint4*>(src) + c + 4);
       const uint4 cl = __ldg(c4 + c), ch = __ldg(c4 + c + 4), sl = __ldg(s4 + c), sh = __ldg(s4 + c + 4);
-      uint4 yl, yh;
-      rope16(xl, xh, cl, ch, sl, sh, yl, yh);
-      reinterpret_cast<uint4*>(dst)[c] = yl;
-      reinterpret_cast<uint4*>(dst)[c + 4] = yh;
+      const uint32_t lo[4] = {xl.x, xl.y, xl.z, xl.w}, hi[4] = {xh.x, xh.y, xh.z, xh.w};
+      const uint32_t cl4[4] = {cl.x, cl.y, cl.z, cl.w}, ch4[4] = {ch.x, ch.y, ch.z, ch.w};
+      const uint32_t sl4[4] = {sl.x, sl.y, sl.z, sl.w}, sh4[4] = {sh.x, sh.y, sh.z, sh.w};
+      uint32_t ylo[4], yhi[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float a0 = e0(lo[w]), a1 = e1(lo[w]), b0 = e0(hi[w]), b1 = e1(hi[w]);
+        ylo[w] = pack_bf16x2(a0 * e0(cl4[w]) - b0 * e0(sl4[w]), a1 * e1(cl4[w]) - b1 * e1(sl4[w]));
+        yhi[w] = pack_bf16x2(b0 * e0(ch4[w]) + a0 * e0(sh4[w]), b1 * e1(ch4[w]) + a1 * e1(sh4[w]));
+      }
+      reinterpret_cast<uint4*>(dst)[c] = make_uint4(ylo[0], ylo[1], ylo[2], ylo[3]);
+      reinterpret_cast<uint4*>(dst)[c + 4] = make_uint4(yhi[0], yhi[1], yhi[2], yhi[3]);
     }
   }
 }
@@ -573,8 +552,6 @@ __device__ __forceinline__ void write_row_slot(const AttnParams& p, const UnitIn
     hdr[2] = ui.head;
     hdr[3] = ui.kv_lo;
     hdr[4] = ui.n_kv;
-    hdr[5] = ui.c;
-    hdr[6] = ui.kv_head;
   }
   int cnt[4] = {0, 0, 0, 0};
   if (ui.c > 1) {
@@ -601,49 +578,8 @@ __device__ __forceinline__ void write_row_slot(const AttnParams& p, const UnitIn
       const int pos = tq - cq + (lk - lq);
       klo = ck + (p.window_left >= 0 ? max(0, pos - p.window_left) : 0);
       khi = ck + (p.window_right >= 0 ? min(lk, pos + p.window_right + 1) : lk);
-      if constexpr (C::kRope) reinterpret_cast<int*>(rows + kTileM)[r] = cq;  // the row's sequence start
     }
     rows[r] = make_int2(klo, khi);
-  }
-}
-
-// In-kernel RoPE of a 128B-swizzled K-major tile of ROWS rows x 64 bf16 in shared memory, in
-// place, by one warp: item (row j, chunk pair c) rotates dims 8c..8c+7 with 8c+32..8c+39
-// (rope16); row j uses position-table row pos(j), clamped to the table. Chunk c of row j sits at
-// j*128 + (c ^ j%8)*16 (the tile base is 1 KB aligned). Table rows come from L2 (the tables are
-// rope_rows x 256 bytes); two items per lane are in flight at a time.
-template <int ROWS, class PosFn>
-__device__ __forceinline__ void rope_tile(uint8_t* tile, const AttnParams& p, int lane, PosFn pos) {
-  constexpr int kItemsPerLane = ROWS * 4 / 32;
-  constexpr int kBatch = 2;
-#pragma unroll 1
-  for (int b0 = 0; b0 < kItemsPerLane; b0 += kBatch) {
-    uint4 xl[kBatch], xh[kBatch], cl[kBatch], ch[kBatch], sl[kBatch], sh[kBatch];
-    uint8_t* rowp[kBatch];
-    int cc[kBatch];
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int item = (b0 + u) * 32 + lane;
-      const int j = item >> 2, c = item & 3;
-      const int pr = min(max(pos(j), 0), p.rope_rows - 1);
-      const uint4* c4 = reinterpret_cast<const uint4*>(p.rope_cos + (long long)pr * p.rope_stride);
-      const uint4* s4 = reinterpret_cast<const uint4*>(p.rope_sin + (long long)pr * p.rope_stride);
-      cl[u] = __ldg(c4 + c);
-      ch[u] = __ldg(c4 + c + 4);
-      sl[u] = __ldg(s4 + c);
-      sh[u] = __ldg(s4 + c + 4);
-      rowp[u] = tile + j * 128;
-      cc[u] = c ^ (j & 7);
-      xl[u] = *reinterpret_cast<const uint4*>(rowp[u] + (cc[u] << 4));
-      xh[u] = *reinterpret_cast<const uint4*>(rowp[u] + ((cc[u] ^ 4) << 4));
-    }
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      uint4 yl, yh;
-      rope16(xl[u], xh[u], cl[u], ch[u], sl[u], sh[u], yl, yh);
-      *reinterpret_cast<uint4*>(rowp[u] + (cc[u] << 4)) = yl;
-      *reinterpret_cast<uint4*>(rowp[u] + ((cc[u] ^ 4) << 4)) = yh;
-    }
   }
 }
 
@@ -671,9 +607,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
   uint64_t* s_full = q_empty + C::QB;
   uint64_t* p_full = s_full + C::NS;
   uint64_t* o_full = p_full + C::NS;  // the last P.V of each unit (epilogue)
-  uint64_t* row_empty = o_full + 1;    // [QB] the softmax warps (and the RoPE warp) took the row slot
-  uint64_t* q_rot = row_empty + C::QB;  // [QB] (ROPE) the Q tile is rotated
-  uint64_t* k_rot = q_rot + C::QB;      // [ST] (ROPE) the K tile is rotated
+  uint64_t* row_empty = o_full + 1;    // [QB] the softmax warps took the unit's row slot
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
 
   const int warp = threadIdx.x >> 5;
@@ -697,11 +631,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       mbar_init(&p_full[i], 4);  // one arrival per softmax warp
     }
     mbar_init(o_full, 1);
-    for (int i = 0; i < C::QB; ++i) mbar_init(&row_empty[i], C::kRope ? 5 : 4);
-    if constexpr (C::kRope) {
-      for (int i = 0; i < C::QB; ++i) mbar_init(&q_rot[i], 1);
-      for (int i = 0; i < C::ST; ++i) mbar_init(&k_rot[i], 1);
-    }
+    for (int i = 0; i < C::QB; ++i) mbar_init(&row_empty[i], 4);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -862,9 +792,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         // The previous unit's last P.Vs go before this unit's first QK: the softmax warps run
         // that unit's epilogue before they can use the new S, so its O is what they wait for.
         while (npend > 0) flush_one();
-        // With in-kernel RoPE the RoPE warp publishes the rotated Q tile (and passes on the
-        // stream's end marker) after the producer's q_full.
-        mbar_wait(C::kRope ? &q_rot[qb] : &q_full[qb], (lu / C::QB) & 1, p.err);
+        mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
         tc_fence_after();
         const int n_kv = reinterpret_cast<const int*>(smem + C::kOffRows + qb * C::kRowSlotBytes)[4];
         if (n_kv < 0) break;
@@ -875,7 +803,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           // With one S buffer the previous P must be consumed first (issue order = execution order).
           if (C::NS == 1)
             while (npend > 0) flush_one();
-          mbar_wait(C::kRope ? &k_rot[st] : &k_full[st], (int)(i / C::ST) & 1, p.err);
+          mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
           tc_fence_after();
           const uint32_t k_addr = smem_base + C::kOffK + st * C::kKVBytes;
 #pragma unroll
@@ -899,51 +827,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         }
       }
       while (npend > 0) flush_one();
-    }
-  } else if (C::kRope && warp == 6) {
-    // ------------------------------------------------------------------ RoPE (in-kernel rotation)
-    // Follows the producer's units and key tiles: rotates each landed Q tile, then each landed K
-    // tile, in shared memory, and publishes them to the MMA warp (q_rot, k_rot). The MMA warp's
-    // QK releases the buffers (q_empty, k_empty) as before, so a stage is never refilled before
-    // its rotation is done. Positions: token - the row's sequence start (from the row slot).
-    uint32_t i = 0;
-    for (int lu = 0;; ++lu) {
-      const int qb = lu % C::QB;
-      mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
-      const int* slot = reinterpret_cast<const int*>(smem + C::kOffRows + qb * C::kRowSlotBytes);
-      const int n_kv = slot[4];
-      if (n_kv < 0) {  // end of the stream: pass the marker on to the MMA warp
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&q_rot[qb]);
-        break;
-      }
-      const int q_row0 = slot[0], nq = slot[1], kv_lo = slot[3], n_seq_item = slot[5];
-      const int* starts = slot + 16 + 2 * kTileM;  // per query row: its sequence start
-      uint8_t* qs = smem + C::kOffQ + qb * C::kQBytes;
-      rope_tile<kTileM>(qs, p, lane, [&](int r) { return r < nq ? q_row0 + r - starts[r] : 0; });
-      fence_proxy_async_smem();  // the rotated rows are visible to the tensor core
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&q_rot[qb]);
-      // Key rows: a packed item's key rows are its query rows (self-attention); a block of one
-      // sequence reads keys of that sequence (rows past its end are masked and clamped).
-      const int seq_start = starts[0];
-      for (int t = 0; t < n_kv; ++t, ++i) {
-        const int st = (int)(i % C::ST);
-        mbar_wait(&k_full[st], (int)(i / C::ST) & 1, p.err);
-        const int kt = kv_lo + t * C::BN;
-        uint8_t* ks = smem + C::kOffK + st * C::kKVBytes;
-        rope_tile<C::BN>(ks, p, lane, [&](int j) {
-          const int tok = kt + j;
-          const int qr = tok - q_row0;
-          const int start = (n_seq_item > 1 && qr >= 0 && qr < kTileM) ? starts[qr] : seq_start;
-          return tok - start;
-        });
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&k_rot[st]);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&row_empty[qb]);  // done with this unit's row slot
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -1504,7 +1387,7 @@ static size_t rope_k_offset(const PeB200AttnParams* p) {
 }
 
 static size_t workspace_bytes_for(const PeB200AttnParams* p) {
-  if (p->rope_cos && !p->rope_positions) return rope_k_offset(p) + (size_t)p->total_k * p->kv_heads * p->head_dim * 2;
+  if (p->rope_cos) return rope_k_offset(p) + (size_t)p->total_k * p->kv_heads * p->head_dim * 2;
   return (size_t)kHeaderBytes + sizeof(WorkItem) * (size_t)item_capacity(p);
 }
 
@@ -1542,12 +1425,9 @@ static int validate(const PeB200AttnParams* p, int level) {
     if (!aligned16(p->rope_cos) || !aligned16(p->rope_sin) || p->rope_stride_token < p->head_dim ||
         (p->rope_stride_token * 2) % 16 != 0)
       return PE_B200_ERR_STRIDE;
-    // Tables are per query token (or position) and applied to key rows of the same index:
-    // self-attention only.
+    // Tables are per query token and applied to key rows of the same index: self-attention only.
     if (p->head_dim != 64 || p->cu_seqlens_k != p->cu_seqlens_q || p->total_k != p->total_q)
       return PE_B200_ERR_UNSUPPORTED;
-    if (p->rope_positions != 0 && p->rope_positions != 1) return PE_B200_ERR_UNSUPPORTED;
-    if (p->rope_positions && p->rope_rows < 1) return PE_B200_ERR_SHAPE;
   }
   return PE_B200_OK;
 }
@@ -1610,10 +1490,6 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   ap.g_tok = p->g_stride_token;
   ap.g_head = p->g_stride_head;
   ap.kv_major = kv_major ? 1 : 0;
-  ap.rope_cos = static_cast<const __nv_bfloat16*>(p->rope_cos);
-  ap.rope_sin = static_cast<const __nv_bfloat16*>(p->rope_sin);
-  ap.rope_stride = p->rope_stride_token;
-  ap.rope_rows = p->rope_rows;
   const long long units = item_capacity(p) * p->heads;
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
@@ -1695,7 +1571,7 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   const DeviceInfo& info = device_info(dev);
   if (info.supported != 1) return PE_B200_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (p->rope_cos && !p->rope_positions) {  // per-token tables (head_dim 64, self-attention): rotate, then attend
+  if (p->rope_cos) {  // rotary tables (validated: head_dim 64, self-attention): rotate, then attend
     uint8_t* ws = static_cast<uint8_t*>(p->workspace);
     __nv_bfloat16* q_rot = reinterpret_cast<__nv_bfloat16*>(ws + rope_q_offset(p));
     __nv_bfloat16* k_rot = reinterpret_cast<__nv_bfloat16*>(ws + rope_k_offset(p));
@@ -1717,7 +1593,7 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
     r.k_stride_head = 64;
     return pe_b200_attn_run(&r, stream);
   }
-  if (p->gate && (gate_as_own_pass() || p->rope_positions)) {
+  if (p->gate && gate_as_own_pass()) {
     PeB200AttnParams ungated = *p;
     ungated.gate = nullptr;
     st = pe_b200_attn_run(&ungated, stream);
@@ -1736,13 +1612,6 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
       case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 0, false, true>>(p, s, info.sms);
       default: return PE_B200_ERR_UNSUPPORTED;
     }
-  }
-  if (p->rope_cos) {  // position tables (validated: head_dim 64, self-attention): rotation in the kernel
-    const bool windowed = (p->window_left >= 0 || p->window_right >= 0) && !p->causal;
-    if (windowed) return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 0, true, false, true, true>>(p, s, info.sms);
-    if (p->max_seqlen_k > 0 && p->max_seqlen_k <= kTileM)
-      return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 0, false, false, true, true>>(p, s, info.sms);
-    return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 0, false, false, true, true>>(p, s, info.sms);
   }
   switch (p->head_dim) {
     case 64: {

@@ -163,7 +163,6 @@ def packed_attention(
     plan: AttentionPlan | None = None,
     gate: Tensor | None = None,
     rope: tuple[Tensor, Tensor] | None = None,
-    rope_positions: bool = False,
 ):
     """Packed variable-length attention on B200.
 
@@ -182,11 +181,6 @@ def packed_attention(
     rotates them (the reference's rotate-half rule of ``apply_rope_bshd``, _kernels/rope.py:140-200,
     used at forward.py:199-205) into its workspace with this library's rope pass, then attends.
     head_dim 64, self-attention (no ``cu_seqlens_k``), no ``plan``.
-    ``rope_positions=True``: ``rope`` holds POSITION tables ``[P, D]`` (the reference's
-    ``rope_tables(max_seqlen)`` before its per-token gather, forward.py:493-510) and token t of a
-    sequence starting at s uses row t - s (clamped to P - 1); the rotation then happens inside
-    the attention kernel on the landed Q and K tiles, with the same rule and roundings, and no
-    rotated copy goes through device memory (``plan`` is allowed).
     """
     _check_qkv(q, k, v)
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
@@ -211,16 +205,13 @@ def packed_attention(
         raise UnsupportedTargetError("out must match q's shape/dtype with a contiguous head_dim")
     if rope is not None:
         cos, sin = rope
-        rows = cos.shape[0] if rope_positions else tq
-        if (cos.ndim != 2 or cos.shape != (rows, dim) or sin.shape != cos.shape or rows < 1
-                or cos.dtype != torch.bfloat16 or sin.dtype != torch.bfloat16 or cos.stride(1) != 1
-                or sin.stride(1) != 1 or cos.stride(0) != sin.stride(0) or cos.device != q.device
-                or sin.device != q.device):
-            raise UnsupportedTargetError("rope tables must be bf16 [Tq, D] (or [P, D] position tables with "
-                                         "rope_positions) with a contiguous D and one row stride")
+        if (cos.shape != (tq, dim) or sin.shape != cos.shape or cos.dtype != torch.bfloat16
+                or sin.dtype != torch.bfloat16 or cos.stride(1) != 1 or sin.stride(1) != 1
+                or cos.stride(0) != sin.stride(0) or cos.device != q.device or sin.device != q.device):
+            raise UnsupportedTargetError("rope tables must be bf16 [Tq, D] with a contiguous D and one row stride")
         if dim != 64 or cu_seqlens_k is not None or tk != tq:
             raise UnsupportedTargetError("rope: head_dim 64 self-attention only")
-        if plan is not None and not rope_positions:
+        if plan is not None:
             raise UnsupportedTargetError("rope calls keep the rotated q/k in their own workspace: omit plan")
     if gate is not None and (gate.shape != q.shape or gate.dtype != torch.bfloat16 or gate.stride(2) != 1
                              or gate.device != q.device):
@@ -252,8 +243,6 @@ def packed_attention(
     if rope is not None:
         params.rope_cos, params.rope_sin = _ptr(rope[0]), _ptr(rope[1])
         params.rope_stride_token = rope[0].stride(0)
-        params.rope_positions = int(bool(rope_positions))
-        params.rope_rows = rope[0].shape[0]
     so = _lib.lib()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device)

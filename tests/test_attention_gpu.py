@@ -398,64 +398,6 @@ def test_fused_rope_matches_rotate_then_attend(lengths, heads, kv_heads, window,
     assert pe.device_error_word() == 0
 
 
-def _position_tables(max_pos, theta, dim=64):
-    """RoPE position tables [max_pos, dim] bf16 (ModernBERT's rotary: theta^(-2i/dim), emb = [f, f]),
-    the reference's rope_tables before its per-token gather (packed_encoders/forward.py:493-510)."""
-    inv = 1.0 / theta ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim)
-    pos = torch.arange(max_pos, dtype=torch.float32)
-    emb = torch.cat((pos[:, None] * inv, pos[:, None] * inv), -1)
-    return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
-
-
-@pytest.mark.parametrize("lengths,heads,kv_heads,window,causal", ROPE_CASES)
-def test_in_kernel_rope_matches_oracle_and_rope_pass(lengths, heads, kv_heads, window, causal):
-    """RoPE inside the attention kernel (position tables, rope_positions=True): against the oracle
-    on the per-token gathered tables (position = index inside the sequence, the position_ids of
-    packed_forward, forward.py:455-457), and bit-identical to the rope-pass mode on those gathered
-    tables (one rotation routine serves both)."""
-    pe = _b200()
-    q, k, v, cu = packed_inputs(lengths, heads, 64, kv_heads=kv_heads, seed=37)
-    cos_p, sin_p = _position_tables(max(max(lengths), 1), 160000.0 if window == (-1, -1) else 10000.0)
-    pos = torch.cat([torch.arange(n) for n in lengths]).long()
-    cos_t, sin_t = cos_p[pos], sin_p[pos]
-    rq, rk = oracle.rope_bshd(q, cos_t, sin_t), oracle.rope_bshd(k, cos_t, sin_t)
-    ref, ref_lse = oracle.attention(rq, rk, v, cu, scale=0.125, window=window, causal=causal)
-    kw = dict(scale=0.125, window=window, causal=causal)
-    dq, dk, dv, dcu = q.cuda(), k.cuda(), v.cuda(), cu.cuda()
-    out, lse = pe.packed_attention(dq, dk, dv, dcu, max(lengths), rope=(cos_p.cuda(), sin_p.cuda()),
-                                   rope_positions=True, return_lse=True, **kw)
-    via_pass = pe.packed_attention(dq, dk, dv, dcu, max(lengths), rope=(cos_t.cuda(), sin_t.cuda()), **kw)
-    torch.cuda.synchronize()
-    what = f"in-kernel rope {lengths[:6]} H{heads}/{kv_heads} w{window} c{causal}"
-    _assert_parity(out, ref, what)
-    _assert_lse(lse, ref_lse, what)
-    assert torch.equal(out, via_pass), what
-    assert pe.device_error_word() == 0
-
-
-def test_in_kernel_rope_on_qkv_views_with_plan():
-    """q, k, v as views of one fused qkv [T, 3, H, D] (forward.py:197-205), position tables shorter
-    than the longest sequence would need are not allowed to matter (rows are clamped; here the
-    table covers every position), and a prebuilt plan reused by two calls."""
-    pe = _b200()
-    lengths, heads = [40, 200, 7, 513, 1, 129], 12
-    total = sum(lengths)
-    gen = torch.Generator().manual_seed(41)
-    qkv = torch.randn(total, 3, heads, 64, generator=gen).to(torch.bfloat16).cuda()
-    cu = torch.tensor([0] + lengths, dtype=torch.int32).cumsum(0, dtype=torch.int32).cuda()
-    cos_p, sin_p = (t.cuda() for t in _position_tables(max(lengths), 10000.0))
-    pos = torch.cat([torch.arange(n) for n in lengths]).long().cuda()
-    for window in ((64, 64), (-1, -1)):
-        plan = pe.ops.plan_attention(qkv[:, 0], qkv[:, 1], cu, max(lengths), window=window)
-        outs = [pe.packed_attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, max(lengths), scale=0.125, window=window,
-                                    rope=(cos_p, sin_p), rope_positions=True, plan=plan) for _ in range(2)]
-        via_pass = pe.packed_attention(qkv[:, 0], qkv[:, 1], qkv[:, 2], cu, max(lengths), scale=0.125, window=window,
-                                       rope=(cos_p[pos], sin_p[pos]))
-        torch.cuda.synchronize()
-        assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], via_pass), window
-        assert plan.error_word() == 0
-
-
 def test_fused_rope_on_qkv_views():
     """q and k as strided views of a fused qkv projection [T, 3, H, D] (forward.py:197-205), windowed
     and global, with strided table views."""
