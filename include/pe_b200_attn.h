@@ -18,7 +18,7 @@
 extern "C" {
 #endif
 
-#define PE_B200_ABI_VERSION 3
+#define PE_B200_ABI_VERSION 4
 
 enum {
   PE_B200_OK = 0,
@@ -179,6 +179,52 @@ int pe_b200_attn_fwd_noalloc(const PeB200AttnParams* p, void* stream);
  * the no-allocation path's view of the workspace error word of pe_b200_attn_fwd).
  */
 int pe_b200_noalloc_error_word(int* out, void* stream);
+
+/*
+ * Backward of packed self-attention (ABI 4): dq, dk, dv of out = attention(q, k, v) given dout,
+ * the forward's out and its natural-log lse [heads, total] (pe_b200_attn_fwd with lse != NULL).
+ * head_dim 64, heads == kv_heads, one cu_seqlens for queries and keys, the forward's window /
+ * causal / scale. bf16 tensors [total, heads, 64] with element strides (token, head), D
+ * contiguous, 16-byte aligned. The workspace (pe_b200_attn_bwd_workspace_size bytes, 256-byte
+ * aligned) holds the tile schedule, an fp32 dq accumulator [total, heads, 64] and two fp32
+ * [heads, total] row vectors. Enqueues the schedule builder, a row pass (rowsum(dout * out)), the
+ * tcgen05 backward kernel and the dq conversion on `stream`. No counterpart in the reference:
+ * its training path keeps SDPA's own backward (packed_encoders/pack.py:231-235).
+ */
+typedef struct PeB200AttnBwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* out;
+  const void* dout;
+  const float* lse;
+  void* dq;
+  void* dk;
+  void* dv;
+  const int32_t* cu_seqlens;
+  int32_t n_seq;
+  int32_t total;
+  int32_t max_seqlen;
+  int32_t heads;
+  int32_t head_dim;
+  int64_t q_stride_token, q_stride_head;
+  int64_t k_stride_token, k_stride_head;
+  int64_t v_stride_token, v_stride_head;
+  int64_t o_stride_token, o_stride_head;
+  int64_t do_stride_token, do_stride_head;
+  int64_t dq_stride_token, dq_stride_head;
+  int64_t dk_stride_token, dk_stride_head;
+  int64_t dv_stride_token, dv_stride_head;
+  float scale;
+  int32_t window_left;
+  int32_t window_right;
+  int32_t causal;
+  void* workspace;
+  size_t workspace_bytes;
+} PeB200AttnBwdParams;
+
+int pe_b200_attn_bwd_workspace_size(const PeB200AttnBwdParams* p, size_t* bytes);
+int pe_b200_attn_bwd(const PeB200AttnBwdParams* p, void* stream);
 
 /*
  * Rotary embedding of q and k into contiguous copies, the reference's BSHD RoPE pass

@@ -10,6 +10,7 @@ from packed_encoders_b200.ops import (
     device_error_word,
     flash_attention_varlen,
     packed_attention,
+    packed_attention_backward,
     packed_short_attention,
     packed_short_attention_supported,
 )
@@ -17,5 +18,6 @@ from packed_encoders_b200.ops import (
 __all__ = [
     "PackedEncodersError", "UnsupportedTargetError", "ValidationError",
     "apply_rope_bshd", "attention_bshd", "device_error_word", "flash_attention_varlen", "packed_attention",
+    "packed_attention_backward",
     "packed_short_attention", "packed_short_attention_supported",
 ]

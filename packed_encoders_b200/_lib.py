@@ -13,7 +13,7 @@ from pathlib import Path
 from packed_encoders_b200.errors import PackedEncodersError
 
 LIB_PATH = Path(__file__).resolve().parent / "libpe_b200.so"
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -41,11 +41,27 @@ class PeB200AttnParams(ctypes.Structure):
     ]
 
 
+class PeB200AttnBwdParams(ctypes.Structure):
+    """Mirror of ``PeB200AttnBwdParams`` (include/pe_b200_attn.h)."""
+
+    _fields_ = [
+        ("q", _p), ("k", _p), ("v", _p), ("out", _p), ("dout", _p), ("lse", _p),
+        ("dq", _p), ("dk", _p), ("dv", _p), ("cu_seqlens", _p),
+        ("n_seq", _i32), ("total", _i32), ("max_seqlen", _i32), ("heads", _i32), ("head_dim", _i32),
+        ("q_stride_token", _i64), ("q_stride_head", _i64), ("k_stride_token", _i64), ("k_stride_head", _i64),
+        ("v_stride_token", _i64), ("v_stride_head", _i64), ("o_stride_token", _i64), ("o_stride_head", _i64),
+        ("do_stride_token", _i64), ("do_stride_head", _i64), ("dq_stride_token", _i64), ("dq_stride_head", _i64),
+        ("dk_stride_token", _i64), ("dk_stride_head", _i64), ("dv_stride_token", _i64), ("dv_stride_head", _i64),
+        ("scale", ctypes.c_float), ("window_left", _i32), ("window_right", _i32), ("causal", _i32),
+        ("workspace", _p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 EXPORTS = (
     "pe_b200_abi_version", "pe_b200_status_string", "pe_b200_last_error_detail", "pe_b200_device_supported",
     "pe_b200_attn_workspace_size", "pe_b200_attn_fwd", "pe_b200_build_schedule", "pe_b200_attn_run",
     "pe_b200_debug_qk", "pe_b200_debug_pv", "pe_b200_rope_qk", "pe_b200_attn_fwd_noalloc",
-    "pe_b200_noalloc_error_word",
+    "pe_b200_noalloc_error_word", "pe_b200_attn_bwd_workspace_size", "pe_b200_attn_bwd",
 )
 
 
@@ -78,6 +94,10 @@ def lib() -> ctypes.CDLL:
     so.pe_b200_attn_fwd_noalloc.argtypes = [ctypes.POINTER(PeB200AttnParams), _p]
     so.pe_b200_noalloc_error_word.restype = ctypes.c_int
     so.pe_b200_noalloc_error_word.argtypes = [ctypes.POINTER(ctypes.c_int), _p]
+    so.pe_b200_attn_bwd_workspace_size.restype = ctypes.c_int
+    so.pe_b200_attn_bwd_workspace_size.argtypes = [ctypes.POINTER(PeB200AttnBwdParams), ctypes.POINTER(ctypes.c_size_t)]
+    so.pe_b200_attn_bwd.restype = ctypes.c_int
+    so.pe_b200_attn_bwd.argtypes = [ctypes.POINTER(PeB200AttnBwdParams), _p]
     so.pe_b200_rope_qk.restype = ctypes.c_int
     so.pe_b200_rope_qk.argtypes = [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _i32, _i32, _i32, _p, _p, _p]
     so.pe_b200_debug_qk.restype = ctypes.c_int

@@ -1497,6 +1497,8 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   return launch_status("attn_fwd_kernel launch");
 }
 
+#include "attn_bwd.cuh"
+
 }  // namespace pe_b200
 
 using namespace pe_b200;
@@ -1636,6 +1638,28 @@ int pe_b200_attn_fwd(const PeB200AttnParams* p, void* stream) {
   st = pe_b200_build_schedule(p, stream);
   if (st != PE_B200_OK) return st;
   return pe_b200_attn_run(p, stream);
+}
+
+int pe_b200_attn_bwd_workspace_size(const PeB200AttnBwdParams* p, size_t* bytes) {
+  const int st = bwd_validate(p, true);
+  if (st != PE_B200_OK) return st;
+  if (!bytes) return PE_B200_ERR_NULL;
+  *bytes = bwd_workspace_bytes(p);
+  return PE_B200_OK;
+}
+
+int pe_b200_attn_bwd(const PeB200AttnBwdParams* p, void* stream) {
+  int st = bwd_validate(p, false);
+  if (st != PE_B200_OK) return st;
+  if (p->n_seq == 0 || p->total == 0) return PE_B200_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PE_B200_ERR_CUDA;
+  const DeviceInfo& info = device_info(dev);
+  if (info.supported != 1) return PE_B200_ERR_DEVICE;
+  const PeB200AttnParams sched = bwd_schedule_params(p);
+  st = pe_b200_build_schedule(&sched, stream);
+  if (st != PE_B200_OK) return st;
+  return bwd_run(p, static_cast<cudaStream_t>(stream), info.sms);
 }
 
 int pe_b200_rope_qk(const void* q, const void* k, int64_t q_stride_token, int64_t q_stride_head,

@@ -430,6 +430,11 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
   return make_float2(__uint_as_float(bx), __uint_as_float(by));
 }
 
+// Four fp32 additions into global memory with one vector reduction (sm_90+).
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));

@@ -184,8 +184,13 @@ def packed_attention(
     """
     _check_qkv(q, k, v)
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
-        raise UnsupportedTargetError("b200 attention is forward-only (no autograd), like the Triton kernel it "
-                                     "replaces (triton_packed_attention.py:171)")
+        if (q.shape[2] != 64 or k.shape[1] != q.shape[1] or cu_seqlens_k is not None or gate is not None
+                or rope is not None or plan is not None or out is not None or return_lse):
+            raise UnsupportedTargetError("b200 attention with autograd: head_dim 64 self-attention with heads == "
+                                         "kv_heads, no gate / rope / plan / out / return_lse")
+        scale_ = float(q.shape[2] ** -0.5 if scale is None else scale)
+        return _PackedAttentionFn.apply(q, k, v, cu_seqlens, int(max_seqlen), scale_,
+                                        tuple(int(w) for w in window), bool(causal))
     cu_k = cu_seqlens if cu_seqlens_k is None else cu_seqlens_k
     for name, cu in (("cu_seqlens", cu_seqlens), ("cu_seqlens_k", cu_k)):
         if cu.dtype != torch.int32 or cu.ndim != 1 or cu.numel() < 1 or cu.device != q.device:
@@ -264,6 +269,72 @@ def packed_attention(
                        "pe_b200_attn_fwd")
             _count(3)
     return (out, lse) if return_lse else out
+
+
+def packed_attention_backward(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, lse: Tensor,
+                              cu_seqlens: Tensor, max_seqlen: int, *, scale: float, window=(-1, -1),
+                              causal: bool = False) -> tuple[Tensor, Tensor, Tensor]:
+    """Gradients (dq, dk, dv) of ``out = packed_attention(q, k, v, cu_seqlens, max_seqlen, scale=scale,
+    window=window, causal=causal)`` given ``dout``, ``out`` and the forward's ``lse`` ([H, T] fp32,
+    ``return_lse=True``): the tcgen05 backward kernel of this library (head_dim 64, heads == kv_heads,
+    one ``cu_seqlens``). The reference has no counterpart: its training path keeps SDPA's backward
+    (packed_encoders/pack.py:231-235)."""
+    for name, t in (("dout", dout), ("out", out)):
+        if t.shape != q.shape or t.dtype != torch.bfloat16 or t.stride(2) != 1 or t.device != q.device:
+            raise UnsupportedTargetError(f"{name} must be bf16 with q's shape and a contiguous head_dim")
+    _check_qkv(q, k, v)
+    tq, heads, dim = q.shape
+    if dim != 64 or k.shape[1] != heads or k.shape[0] != tq:
+        raise UnsupportedTargetError("b200 backward: head_dim 64 self-attention with heads == kv_heads")
+    if lse.shape != (heads, tq) or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise UnsupportedTargetError("lse must be the forward's contiguous fp32 [H, T]")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.ndim != 1 or not cu_seqlens.is_contiguous():
+        raise UnsupportedTargetError("cu_seqlens must be a contiguous 1-D int32 tensor")
+    dq, dk, dv = (torch.empty_like(t, memory_format=torch.contiguous_format) for t in (q, k, v))
+    n_seq = cu_seqlens.numel() - 1
+    if tq == 0 or n_seq == 0:
+        return dq.zero_(), dk.zero_(), dv.zero_()
+    params = _lib.PeB200AttnBwdParams(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), out=_ptr(out), dout=_ptr(dout), lse=_ptr(lse), dq=_ptr(dq), dk=_ptr(dk),
+        dv=_ptr(dv), cu_seqlens=_ptr(cu_seqlens), n_seq=n_seq, total=tq, max_seqlen=int(max_seqlen), heads=heads,
+        head_dim=dim, q_stride_token=q.stride(0), q_stride_head=q.stride(1), k_stride_token=k.stride(0),
+        k_stride_head=k.stride(1), v_stride_token=v.stride(0), v_stride_head=v.stride(1),
+        o_stride_token=out.stride(0), o_stride_head=out.stride(1), do_stride_token=dout.stride(0),
+        do_stride_head=dout.stride(1), dq_stride_token=dq.stride(0), dq_stride_head=dq.stride(1),
+        dk_stride_token=dk.stride(0), dk_stride_head=dk.stride(1), dv_stride_token=dv.stride(0),
+        dv_stride_head=dv.stride(1), scale=float(scale), window_left=int(window[0]), window_right=int(window[1]),
+        causal=int(bool(causal)))
+    so = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(so.pe_b200_attn_bwd_workspace_size(ctypes.byref(params), ctypes.byref(nbytes)), "bwd workspace size")
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device)
+    params.workspace, params.workspace_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device)
+        _lib.check(so.pe_b200_attn_bwd(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)), "pe_b200_attn_bwd")
+    _count(5)
+    return dq, dk, dv  # the workspace returns to torch's stream-ordered allocator
+
+
+class _PackedAttentionFn(torch.autograd.Function):
+    """packed_attention with a backward on this library's kernels (head_dim 64 self-attention)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, scale, window, causal):
+        with torch.no_grad():
+            out, lse = packed_attention(q, k, v, cu_seqlens, max_seqlen, scale=scale, window=window, causal=causal,
+                                        return_lse=True)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens)
+        ctx.cfg = (max_seqlen, scale, window, causal)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse, cu = ctx.saved_tensors
+        max_seqlen, scale, window, causal = ctx.cfg
+        dq, dk, dv = packed_attention_backward(dout.contiguous(), q, k, v, out, lse, cu, max_seqlen, scale=scale,
+                                               window=window, causal=causal)
+        return dq, dk, dv, None, None, None, None, None
 
 
 def device_error_word(device: torch.device | int | None = None) -> int:

@@ -1,0 +1,111 @@
+"""The tcgen05 backward (packed_attention_backward / autograd through packed_attention) against
+an fp32 autograd reference of the same masked attention, per sequence (GPU).
+
+Bars: the gradients are computed from bf16 P and dS (as FlashAttention's backward does), so
+they are compared relative to the gradient's own scale: max |ours - ref| <= 2e-2 * max |ref| and
+per-row cosine >= 0.999 on rows whose reference is not zero. Each test prints its errors.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import packed_inputs
+
+pytestmark = pytest.mark.gpu
+
+REL = 2e-2
+MIN_COS = 0.999
+
+
+def _reference_grads(q, k, v, cu, dout, *, scale, window, causal):
+    """fp32 autograd of softmax(scale q k^T + band mask) v per sequence (the band rule of
+    packed_encoders/runtime/attention.py:157-170)."""
+    qf, kf, vf = (t.detach().float().cpu().requires_grad_() for t in (q, k, v))
+    outs = []
+    cuh = cu.tolist()
+    left, right = window
+    right = 0 if causal else right
+    for a, b in zip(cuh, cuh[1:]):
+        n = b - a
+        if n == 0:
+            continue
+        i = torch.arange(n)[:, None]
+        j = torch.arange(n)[None, :]
+        ok = torch.ones(n, n, dtype=torch.bool)
+        if left >= 0:
+            ok &= (i - j) <= left
+        if right >= 0:
+            ok &= (j - i) <= right
+        s = torch.einsum("qhd,khd->hqk", qf[a:b], kf[a:b]) * scale
+        s = s.masked_fill(~ok, float("-inf"))
+        outs.append(torch.einsum("hqk,khd->qhd", s.softmax(-1), vf[a:b]))
+    out = torch.cat(outs)
+    out.backward(dout.float().cpu())
+    return out.detach(), qf.grad, kf.grad, vf.grad
+
+
+def _check(name, got, ref):
+    got, ref = got.float().cpu(), ref.float().cpu()
+    assert torch.isfinite(got).all(), f"{name}: non-finite"
+    scale = ref.abs().max().item()
+    err = (got - ref).abs().max().item()
+    rows = ref.flatten(1)
+    keep = rows.abs().amax(1) > 0
+    cos = torch.nn.functional.cosine_similarity(got.flatten(1)[keep], rows[keep], dim=1)
+    cmin = cos.min().item() if cos.numel() else 1.0
+    print(f"PARITY {name}: max_abs={err:.5f} ref_max={scale:.4f} rel={err / max(scale, 1e-12):.5f} min_cos={cmin:.6f}")
+    assert err <= REL * scale, f"{name}: {err:.4g} > {REL} x {scale:.4g}"
+    assert cmin >= MIN_COS, f"{name}: min cosine {cmin:.6f}"
+
+
+CASES = [
+    # (lengths, heads, window, causal)
+    ([300, 7, 129, 1000, 64, 1], 4, (-1, -1), False),
+    ([300, 7, 129, 1000, 64, 1], 4, (64, 64), False),
+    ([300, 7, 129, 1000, 64, 1], 4, (-1, -1), True),
+    ([17, 250, 9, 0, 128], 2, (16, 3), False),
+    ([30] * 40 + [5, 100], 3, (-1, -1), False),
+    ([2000, 40], 2, (-1, -1), False),
+]
+
+
+@pytest.mark.parametrize("lengths,heads,window,causal", CASES)
+def test_backward_matches_fp32_autograd(lengths, heads, window, causal):
+    import packed_encoders_b200 as pe
+
+    q, k, v, cu = packed_inputs(lengths, heads, 64, seed=51)
+    gen = torch.Generator().manual_seed(52)
+    dout = torch.randn(q.shape, generator=gen).to(torch.bfloat16)
+    scale = 0.125
+    dq_, dk_, dv_, dcu = q.cuda(), k.cuda(), v.cuda(), cu.cuda()
+    out, lse = pe.packed_attention(dq_, dk_, dv_, dcu, max(lengths), scale=scale, window=window, causal=causal,
+                                   return_lse=True)
+    dq, dk, dv = pe.packed_attention_backward(dout.cuda(), dq_, dk_, dv_, out, lse, dcu, max(lengths), scale=scale,
+                                              window=window, causal=causal)
+    torch.cuda.synchronize()
+    assert pe.device_error_word() == 0
+    _, rdq, rdk, rdv = _reference_grads(q, k, v, cu, dout, scale=scale, window=window, causal=causal)
+    what = f"{lengths[:6]} H{heads} w{window} c{causal}"
+    _check(f"dq {what}", dq, rdq)
+    _check(f"dk {what}", dk, rdk)
+    _check(f"dv {what}", dv, rdv)
+
+
+def test_autograd_through_packed_attention():
+    """packed_attention on grad-requiring q/k/v runs the forward with LSE and this backward."""
+    import packed_encoders_b200 as pe
+
+    lengths = [200, 33, 700]
+    q, k, v, cu = packed_inputs(lengths, 4, 64, seed=53, device="cuda")
+    q, k, v = (t.clone().requires_grad_() for t in (q, k, v))
+    dout = torch.randn(q.shape, device="cuda", generator=torch.Generator("cuda").manual_seed(54)).to(torch.bfloat16)
+    out = pe.packed_attention(q, k, v, cu, max(lengths), scale=0.125, window=(64, 64))
+    out.backward(dout)
+    with torch.no_grad():
+        o2, lse = pe.packed_attention(q, k, v, cu, max(lengths), scale=0.125, window=(64, 64), return_lse=True)
+        grads = pe.packed_attention_backward(dout, q, k, v, o2, lse, cu, max(lengths), scale=0.125, window=(64, 64))
+    torch.cuda.synchronize()
+    for got, want in zip((q.grad, k.grad, v.grad), grads):
+        assert torch.equal(got, want)

@@ -63,20 +63,49 @@ def test_workspace_size_and_validation():
     assert _size(_params(total_k=0))[0] == -2
 
 
-def test_struct_layout_matches_header(tmp_path):
-    """The ctypes mirror has the C compiler's offsets for every field of PeB200AttnParams."""
-    P = _lib.PeB200AttnParams
+@pytest.mark.parametrize("struct", ["PeB200AttnParams", "PeB200AttnBwdParams"])
+def test_struct_layout_matches_header(tmp_path, struct):
+    """The ctypes mirror has the C compiler's offsets for every field of the parameter blocks."""
+    P = getattr(_lib, struct)
     names = [f[0] for f in P._fields_]
     src = tmp_path / "layout.c"
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "pe_b200_attn.h"\nint main(void) {\n'
-                   + "".join(f'  printf("%zu\\n", offsetof(PeB200AttnParams, {n}));\n' for n in names)
-                   + '  printf("%zu\\n", sizeof(PeB200AttnParams));\n  return 0;\n}\n')
+                   + "".join(f'  printf("%zu\\n", offsetof({struct}, {n}));\n' for n in names)
+                   + f'  printf("%zu\\n", sizeof({struct}));\n  return 0;\n}}\n')
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
     c_offsets = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True,
                                                 text=True).stdout.split()]
     assert c_offsets[:-1] == [getattr(P, n).offset for n in names]
     assert c_offsets[-1] == ctypes.sizeof(P)
+
+
+def test_backward_validation_without_touching_cuda():
+    """The backward's host checks: head_dim 64 only, workspace size and alignment, strides."""
+    P = _lib.PeB200AttnBwdParams
+    so = _lib.lib()
+
+    def size(**kw):
+        base = dict(n_seq=3, total=500, max_seqlen=300, heads=4, head_dim=64, scale=0.125, window_left=-1,
+                    window_right=-1, causal=0)
+        base.update(kw)
+        n = ctypes.c_size_t(0)
+        return so.pe_b200_attn_bwd_workspace_size(ctypes.byref(P(**base)), ctypes.byref(n)), n.value
+
+    status, n = size()
+    assert status == 0 and n >= 500 * 4 * 64 * 4 + 2 * 500 * 4 * 4
+    assert size(head_dim=128)[0] == -8
+    assert size(window_left=-3)[0] == -4
+    full = dict(n_seq=3, total=500, max_seqlen=300, heads=4, head_dim=64, scale=0.125, window_left=-1,
+                window_right=-1, causal=0, q=16, k=16, v=16, out=16, dout=16, lse=16, dq=16, dk=16, dv=16,
+                cu_seqlens=16, workspace=256, workspace_bytes=n)
+    for prefix in ("q", "k", "v", "o", "do", "dq", "dk", "dv"):
+        full[f"{prefix}_stride_token"], full[f"{prefix}_stride_head"] = 256, 64
+    assert so.pe_b200_attn_bwd(ctypes.byref(P(**{**full, "workspace_bytes": n - 1})), None) == -5
+    assert so.pe_b200_attn_bwd(ctypes.byref(P(**{**full, "workspace": 128})), None) == -5
+    assert so.pe_b200_attn_bwd(ctypes.byref(P(**{**full, "dk": 24})), None) == -3
+    assert so.pe_b200_attn_bwd(ctypes.byref(P(**{**full, "dv_stride_token": 4})), None) == -3
+    assert so.pe_b200_attn_bwd(ctypes.byref(P(**{**full, "lse": None})), None) == -1
 
 
 def test_gate_stride_validation_without_touching_cuda():
