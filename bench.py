@@ -493,6 +493,10 @@ def run_b200(args):
         except Exception as exc:  # noqa: BLE001
             record["config3_rope"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
         try:
+            record["config3_backward"] = backward_layers(pe, wl)
+        except Exception as exc:  # noqa: BLE001
+            record["config3_backward"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
+        try:
             record["config4_full_forward"] = config4_forward(pe)
         except Exception as exc:  # noqa: BLE001
             record["config4_full_forward"] = {"failed": f"{type(exc).__name__}: {str(exc)[:120]}"}
@@ -807,6 +811,48 @@ def rope_fusion(pe, wl, iters=10):
         res[kind] = r
         del cos, sin, cos_p, sin_p
     del qkv, view
+    return res
+
+
+def backward_layers(pe, wl, iters=5):
+    """Config 3 layers (512 documents, 16 x 64, global and +-64) backward: this library's
+    packed_attention_backward against FlashAttention-2's varlen backward on the same inputs and
+    dout. FLOP = 2.5 x the useful forward FLOP (five matmuls of the recomputing backward against
+    two of the forward); L2 flushed between calls."""
+    res = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    w = wl.config3("mix")
+    q, k, v = wl.make_qkv(w.lengths, w.heads, w.kv_heads, w.head_dim, seed=1)
+    dout = torch.randn(q.shape, device="cuda", generator=torch.Generator("cuda").manual_seed(3)).to(torch.bfloat16)
+    cu = w.cu_seqlens().cuda()
+    try:
+        from flash_attn import flash_attn_varlen_func
+    except Exception as exc:  # noqa: BLE001
+        flash_attn_varlen_func = None
+        res["fa2"] = f"unavailable: {type(exc).__name__}"
+    for kind, (window, causal) in (("global", wl.GLOBAL), ("local", wl.LOCAL64)):
+        out, lse = pe.packed_attention(q, k, v, cu, max(w.lengths), scale=w.scale, window=window, causal=causal,
+                                       return_lse=True)
+        fn = lambda: pe.packed_attention_backward(dout, q, k, v, out, lse, cu, max(w.lengths), scale=w.scale,
+                                                  window=window, causal=causal)
+        ms = _time_call(fn, iters, flush)
+        flops = 2.5 * wl.useful_flops(w.lengths, w.heads, w.head_dim, window, causal)
+        r = {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 2)}
+        if flash_attn_varlen_func is not None:
+            try:
+                qg, kg, vg = (t.detach().clone().requires_grad_() for t in (q, k, v))
+                o = flash_attn_varlen_func(qg, kg, vg, cu, cu, max(w.lengths), max(w.lengths), softmax_scale=w.scale,
+                                           causal=causal, window_size=window)
+                fa = lambda: torch.autograd.grad(o, (qg, kg, vg), dout, retain_graph=True)
+                fms = _time_call(fa, iters, flush)
+                r["fa2_ms"] = round(fms, 4)
+                r["speedup_vs_fa2"] = round(fms / ms, 3)
+                del qg, kg, vg, o
+            except Exception as exc:  # noqa: BLE001
+                r["fa2"] = f"failed: {type(exc).__name__}: {str(exc)[:80]}"
+        res[kind] = r
+        del out, lse
+    del q, k, v, dout
     return res
 
 
