@@ -38,8 +38,8 @@ sys.path.insert(0, str(ROOT))
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one full-size attn_fwd_kernel launch (config 3
 # global layer, all 512 documents), from a one-pass ncu capture of
-# `python bench.py --case config3-global --iters 2`: 7.54 GB read + 0.903 GB written.
-NCU_TRAFFIC_GLOBAL = 7.54e9 + 0.903e9
+# `python bench.py --case config3-global --iters 2`: 3.668 GB read + 0.899 GB written.
+NCU_TRAFFIC_GLOBAL = 3.668e9 + 0.899e9
 
 
 def _env_int(name, default):
@@ -942,10 +942,11 @@ def run_reference(args):
 
 
 def run_case(args):
-    """Profiling helper: ``--case NAME --iters N [--seqs S] [--rope] [--gate]`` launches one
-    configuration N times (no timing output), e.g. for an ncu capture of a small case of the same
+    """Profiling helper: ``--case NAME --iters N [--seqs S] [--rope] [--gate] [--backward]`` launches
+    one configuration N times (no timing output), e.g. for an ncu capture of a small case of the same
     kernel. ``--rope``: q/k/v are views of one packed qkv and the call applies RoPE (head_dim 64);
-    ``--gate``: the call applies the output gate."""
+    ``--gate``: the call applies the output gate; ``--backward``: one forward with LSE, then N
+    backward calls on it."""
     import packed_encoders_b200 as pe
     from packed_encoders_b200 import workloads as wl
 
@@ -970,8 +971,17 @@ def run_case(args):
     if args.gate:
         extra["gate"] = torch.randn(q.shape, device="cuda").to(torch.bfloat16)
     out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    for _ in range(args.iters):
-        pe.packed_attention(q, k, v, cu, max(lengths), scale=w.scale, window=window, causal=causal, out=out, **extra)
+    if args.backward:
+        out, lse = pe.packed_attention(q, k, v, cu, max(lengths), scale=w.scale, window=window, causal=causal,
+                                       return_lse=True)
+        dout = torch.randn(q.shape, device="cuda", generator=torch.Generator("cuda").manual_seed(3)).to(q.dtype)
+        for _ in range(args.iters):
+            pe.packed_attention_backward(dout, q, k, v, out, lse, cu, max(lengths), scale=w.scale, window=window,
+                                         causal=causal)
+    else:
+        for _ in range(args.iters):
+            pe.packed_attention(q, k, v, cu, max(lengths), scale=w.scale, window=window, causal=causal, out=out,
+                                **extra)
     torch.cuda.synchronize()
     print(json.dumps({"case": args.case, "tokens": sum(lengths), "seqs": len(lengths), "iters": args.iters,
                       "device_error_word": pe.device_error_word()}))
@@ -984,6 +994,7 @@ def main():
     ap.add_argument("--seqs", type=int, default=0, help="with --case: use only the first SEQS sequences")
     ap.add_argument("--rope", action="store_true", help="with --case: q/k/v views of one qkv, RoPE in the call")
     ap.add_argument("--gate", action="store_true", help="with --case: output gate in the call")
+    ap.add_argument("--backward", action="store_true", help="with --case: one forward, then --iters backward calls")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
