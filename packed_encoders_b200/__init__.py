@@ -8,6 +8,7 @@ from packed_encoders_b200.ops import (
     apply_rope_bshd,
     attention_bshd,
     device_error_word,
+    flash_attention,
     flash_attention_varlen,
     packed_attention,
     packed_attention_backward,
@@ -17,7 +18,7 @@ from packed_encoders_b200.ops import (
 
 __all__ = [
     "PackedEncodersError", "UnsupportedTargetError", "ValidationError",
-    "apply_rope_bshd", "attention_bshd", "device_error_word", "flash_attention_varlen", "packed_attention",
+    "apply_rope_bshd", "attention_bshd", "device_error_word", "flash_attention", "flash_attention_varlen", "packed_attention",
     "packed_attention_backward",
     "packed_short_attention", "packed_short_attention_supported",
 ]

@@ -21,8 +21,14 @@ After ``install()``, the reference's own entry points run on the B200 kernels un
   (pack.py:161-192) and ``forward._resolve_eager_backend`` (forward.py:301-331, the branch that
   consults the calibrated Triton-vs-FA policy of attention_dispatch.py:129-205, eager and
   ``for_cuda_graph`` alike) stop there, so ``pe.pack(model)`` with no backend argument runs on
-  these kernels. Training (grad enabled) keeps the reference's own resolution: the kernels are
-  forward-only, like the Triton kernel they replace.
+  these kernels. A leaf-level ``"auto"`` resolved while grad is enabled keeps the reference's own
+  resolution.
+* training: with grad enabled the ModernBERT layer takes its BHSD path (RoPE outside the
+  attention call, ``ops.use_bshd_rope_flash`` is False), and ``ops.attention`` with ``"b200"``
+  runs this library's forward and backward kernels (head_dim 64): packed batches through
+  ``flash_attention_varlen`` (the eager packed training forward, forward.py:634-657), unpadded
+  rectangular batches through ``flash_attention`` (the training graph of train_graph.py:170-181,
+  which ``pe.pack(..., train_cuda_graph=True)`` builds with the pack's backend, pack.py:216-238).
 
 There is no policy and no fallback: ``"b200"`` always means these kernels; anything they do
 not implement raises ``UnsupportedTargetError``.
@@ -53,8 +59,8 @@ def _reference_bshd(q, k, v, *, window, scaling, backend="flash", cu_seqlens=Non
 def _check_bshd(q, k, v, *, window, scaling, backend="flash", cu_seqlens=None, max_seqlen=None):
     if q.ndim != 4 or q.shape != k.shape or q.shape != v.shape:
         raise UnsupportedTargetError("attention piece requires equal Q/K/V shapes")
-    if cu_seqlens is None or q.shape[0] != 1 or cu_seqlens.dtype != torch.int32 or max_seqlen is None:
-        raise UnsupportedTargetError("b200 BSHD attention is the packed form: B=1, int32 cu_seqlens, max_seqlen")
+    if cu_seqlens is not None and (q.shape[0] != 1 or cu_seqlens.dtype != torch.int32 or max_seqlen is None):
+        raise UnsupportedTargetError("packed b200 BSHD attention: B=1, int32 cu_seqlens, max_seqlen")
     if scaling <= 0:
         raise UnsupportedTargetError("unsupported attention scale")
 
@@ -168,8 +174,8 @@ def install() -> None:
     @functools.wraps(orig_attention)
     def attention(q, k, v, *, mask, window, scaling, backend, cu_seqlens=None, max_seqlen=None):
         if backend == BACKEND:
-            if cu_seqlens is None:
-                raise UnsupportedTargetError("the b200 backend serves the packed (cu_seqlens) path only")
+            if cu_seqlens is None:  # the rectangular (unpadded) form, e.g. the training graph's forward
+                return b200_ops.flash_attention(q, k, v, window, scaling)
             return b200_ops.flash_attention_varlen(q, k, v, cu_seqlens, max_seqlen, window, scaling)
         return orig_attention(q, k, v, mask=mask, window=window, scaling=scaling, backend=backend,
                               cu_seqlens=cu_seqlens, max_seqlen=max_seqlen)
@@ -232,12 +238,16 @@ def install() -> None:
             return orig_prepare(encoder, attention_backend=attention_backend, cuda_graph=cuda_graph,
                                 cuda_graph_seq_cutoff=cuda_graph_seq_cutoff, **kwargs)
         # "sdpa" passes the name check with no optional dependency; the state is then switched
-        # to b200 before any graph is captured.
-        state = orig_prepare(encoder, attention_backend="sdpa", cuda_graph=False,
+        # to b200 before any runner is built, so the inference graphs and the training graph
+        # (pack.py:216-238 builds it with the state's backend) run on these kernels.
+        train_cuda_graph = kwargs.pop("train_cuda_graph", False)
+        state = orig_prepare(encoder, attention_backend="sdpa", cuda_graph=False, train_cuda_graph=False,
                              cuda_graph_seq_cutoff=cuda_graph_seq_cutoff, **kwargs)
         state.attention_backend = BACKEND
         if cuda_graph:
             pack._enable_graphs(encoder, state, cuda_graph, cuda_graph_seq_cutoff)
+        if train_cuda_graph:
+            pack._enable_train_graphs(encoder, state, train_cuda_graph, cuda_graph_seq_cutoff)
         return state
 
     ops.use_bshd_rope_flash = use_bshd_rope_flash

@@ -368,17 +368,46 @@ def packed_short_attention_supported(q, k, v, cu_seqlens, max_seqlen, *, half_wi
             and not torch.is_grad_enabled())
 
 
+def _row_segments(batch: int, seq: int, device: torch.device) -> Tensor:
+    """cu_seqlens of a rectangular batch read as ``batch`` sequences of ``seq`` tokens each; built on
+    the device with no host synchronisation, so a CUDA-graph capture can contain it."""
+    return torch.arange(0, (batch + 1) * seq, seq, dtype=torch.int32, device=device)
+
+
+def _rectangular(q: Tensor, k: Tensor, v: Tensor, window, scaling) -> Tensor:
+    """``[B, S, H, D]`` q/k/v of an unpadded batch: every row is one sequence of S tokens (the
+    reference's dense flash call makes the same assumption, ops.py:404-409). Returns ``[B, S, H*D]``."""
+    b, s, h, d = q.shape
+    if k.shape[:2] != (b, s) or v.shape[:2] != (b, s):
+        raise UnsupportedTargetError("rectangular b200 attention needs q, k and v with the same [B, S]")
+    flat = [t.reshape(b * s, t.shape[2], d) for t in (q, k, v)]  # a view when the rows are evenly strided
+    out = packed_attention(*flat, _row_segments(b, s, q.device), s, scale=scaling, window=tuple(window))
+    return out.reshape(b, s, h * d)
+
+
 def attention_bshd(q, k, v, *, window, scaling, cu_seqlens=None, max_seqlen=None, backend="b200"):
-    """Drop-in for packed_encoders.ops.attention_bshd (ops.py:502-538) on the packed path:
-    ``[1, T, H, D]`` views in, ``[1, T, H*D]`` out. Only the packed (``cu_seqlens``) form is
-    served; a rectangular call is the reference's dense path and is refused here."""
+    """Drop-in for packed_encoders.ops.attention_bshd (ops.py:502-538): ``[1, T, H, D]`` views and
+    ``cu_seqlens`` in, ``[1, T, H*D]`` out; without ``cu_seqlens`` a ``[B, S, H, D]`` unpadded batch
+    (each row one sequence, like the reference's dense flash call) in, ``[B, S, H*D]`` out."""
     if backend != "b200":
         raise UnsupportedTargetError(f"packed_encoders_b200.attention_bshd serves backend 'b200', not {backend!r}")
     if cu_seqlens is None:
-        raise UnsupportedTargetError("b200 attention_bshd needs cu_seqlens (packed varlen batch)")
+        if q.ndim != 4:
+            raise UnsupportedTargetError("rectangular b200 attention_bshd takes [B, S, H, D] q/k/v")
+        return _rectangular(q, k, v, window, scaling)
     qf, kf, vf = q.squeeze(0), k.squeeze(0), v.squeeze(0)
     out = packed_attention(qf, kf, vf, cu_seqlens, int(max_seqlen), scale=scaling, window=tuple(window))
     return out.reshape(1, out.shape[0], -1)
+
+
+def flash_attention(q, k, v, window, scaling):
+    """Drop-in for packed_encoders.ops.flash_attention (ops.py:404-430): ``[B, H, S, D]`` views of an
+    unpadded batch in (every row one sequence of S tokens; the window as given per layer),
+    ``[B, S, H*D]`` out. Differentiable (head_dim 64), so the reference's rectangular training graph
+    (train_graph.py:170-181) can run on these kernels."""
+    if q.ndim != 4:
+        raise UnsupportedTargetError("b200 flash_attention takes [B, H, S, D] q/k/v")
+    return _rectangular(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), window, scaling)
 
 
 def flash_attention_varlen(q, k, v, cu_seqlens, max_seqlen, window, scaling):

@@ -209,6 +209,28 @@ def test_flash_attention_varlen_drop_in(window):
     _assert_parity(out.view(total, heads, 64), ref, f"flash_attention_varlen w{window}")
 
 
+@pytest.mark.parametrize("window", [(-1, -1), (64, 64)])
+def test_rectangular_drop_ins(window):
+    """ops.flash_attention (packed_encoders/ops.py:404-430): [B, H, S, D] views of an unpadded batch
+    in, every row one sequence, [B, S, H*D] out; and attention_bshd's rectangular form ([B, S, H, D]
+    in). Both against the oracle run per row."""
+    pe = _b200()
+    b, heads, s = 3, 4, 200
+    gen = torch.Generator().manual_seed(31)
+    qkv = torch.randn(b, s, 3, heads, 64, generator=gen).to(torch.bfloat16)
+    q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # [B, H, S, D] views
+    out = pe.flash_attention(q.cuda(), k.cuda(), v.cuda(), window, 0.125)
+    dq, dk, dv = (qkv[:, :, i].cuda() for i in range(3))  # [B, S, H, D] strided views
+    out_bshd = pe.attention_bshd(dq, dk, dv, window=window, scaling=0.125)
+    torch.cuda.synchronize()
+    assert out.shape == (b, s, heads * 64) and out_bshd.shape == (b, s, heads * 64)
+    cu = torch.arange(0, (b + 1) * s, s, dtype=torch.int32)
+    flat = [qkv[:, :, i].reshape(b * s, heads, 64) for i in range(3)]
+    ref, _ = oracle.attention(*flat, cu, scale=0.125, window=window)
+    _assert_parity(out.reshape(b * s, heads, 64), ref, f"flash_attention w{window}")
+    _assert_parity(out_bshd.reshape(b * s, heads, 64), ref, f"attention_bshd rectangular w{window}")
+
+
 @pytest.mark.parametrize("logit_scale", [0.01, 1.0, 8.0])
 def test_softmax_stability_and_determinism(logit_scale):
     """tests/test_packed_short_attention.py:97-109: finite at extreme logit scales and bitwise

@@ -123,6 +123,26 @@ def test_pack_without_backend_prepares_b200_on_sm100(installed, monkeypatch):
     model = ModernBertModel(cfg).eval()
     state = pack._prepare_modernbert(model, validate=False)
     assert state.attention_backend == "b200"
+    assert state.train_graph_runner is None
+
+
+def test_train_graph_runner_is_built_on_b200(installed, monkeypatch):
+    """pack(..., train_cuda_graph=True) builds the training graph runner with the pack's backend
+    (pack.py:216-238); with "b200" the runner's forward calls the b200 attention."""
+    import importlib
+
+    pack = importlib.import_module("packed_encoders.pack")
+    _fake_device(monkeypatch, (10, 0), "NVIDIA B200")
+    monkeypatch.setattr(pack, "_require_cuda", lambda encoder: None)
+    from transformers import ModernBertConfig, ModernBertModel
+
+    cfg = ModernBertConfig(vocab_size=512, hidden_size=128, intermediate_size=192, num_hidden_layers=3,
+                           num_attention_heads=2, local_attention=128, global_attn_every_n_layers=3,
+                           max_position_embeddings=1024, pad_token_id=0)
+    model = ModernBertModel(cfg).eval()
+    state = pack._prepare_modernbert(model, validate=False, train_cuda_graph=True)
+    assert state.attention_backend == "b200"
+    assert state.train_graph_runner is not None and state.train_graph_runner._backend == "b200"
 
 
 def test_candidate_forms_call_the_kernels(installed, monkeypatch):
@@ -158,18 +178,52 @@ def test_b200_piece_contract(installed):
 
     piece = installed.b200_attention_bshd_piece()
     assert piece.contract == BSHD
-    q = torch.zeros(1, 10, 2, 64)
-    with pytest.raises(Exception):  # the rectangular form is not served
-        piece.check(q, q, q, window=(-1, -1), scaling=0.125, backend="flash")
+    q = torch.zeros(2, 10, 2, 64)
+    piece.check(q, q, q, window=(-1, -1), scaling=0.125, backend="flash")  # rectangular: rows are sequences
+    with pytest.raises(Exception):
+        piece.check(q, q[:, :5], q, window=(-1, -1), scaling=0.125, backend="flash")
+    with pytest.raises(Exception):  # the packed form is one row
+        piece.check(q, q, q, window=(-1, -1), scaling=0.125, cu_seqlens=torch.tensor([0, 10], dtype=torch.int32),
+                    max_seqlen=10)
 
 
-def test_attention_leaf_refuses_rectangular_b200(installed):
+def _record_packed(monkeypatch):
+    from packed_encoders_b200 import ops as b200_ops
+
+    calls = []
+
+    def recorder(q, k, v, cu, max_len, **kw):
+        calls.append((q, cu, max_len, kw))
+        return q.clone()
+
+    monkeypatch.setattr(b200_ops, "packed_attention", recorder)
+    return calls
+
+
+def test_attention_leaf_serves_rectangular_b200(installed, monkeypatch):
+    """A rectangular [B, H, S, D] call with backend "b200" (the training graph's forward,
+    train_graph.py:170-181) runs as B sequences of S tokens: cu_seqlens 0, S, 2S, ..., built on
+    the device, and the output comes back as [B, S, H*D] like the reference's flash call."""
     from packed_encoders import ops
-    from packed_encoders_b200.errors import UnsupportedTargetError
 
-    q = torch.zeros(1, 2, 10, 64)
-    with pytest.raises(UnsupportedTargetError):
-        ops.attention(q, q, q, mask=None, window=(-1, -1), scaling=0.125, backend="b200")
+    calls = _record_packed(monkeypatch)
+    q = torch.randn(3, 2, 10, 64)
+    out = ops.attention(q, q, q, mask=None, window=(64, 64), scaling=0.125, backend="b200")
+    qf, cu, max_len, kw = calls[-1]
+    assert qf.shape == (30, 2, 64) and torch.equal(qf, q.transpose(1, 2).reshape(30, 2, 64))
+    assert cu.dtype == torch.int32 and cu.tolist() == [0, 10, 20, 30] and max_len == 10
+    assert kw["window"] == (64, 64) and kw["scale"] == 0.125
+    assert out.shape == (3, 10, 128) and torch.equal(out, q.transpose(1, 2).reshape(3, 10, 128))
+
+
+def test_attention_bshd_serves_rectangular_b200(installed, monkeypatch):
+    from packed_encoders import ops
+
+    calls = _record_packed(monkeypatch)
+    q = torch.randn(2, 7, 2, 64)
+    out = ops.attention_bshd(q, q, q, window=(-1, -1), scaling=0.125, backend="b200")
+    assert calls[-1][1].tolist() == [0, 7, 14] and calls[-1][2] == 7
+    assert out.shape == (2, 7, 128)
 
 
 def test_pieces_replace_attention_and_rope_slots(installed, monkeypatch):

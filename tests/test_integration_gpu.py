@@ -37,11 +37,11 @@ def b200():
     return install
 
 
-def _tiny_modernbert(seed=0):
+def _tiny_modernbert(seed=0, layers=3):
     from transformers import ModernBertConfig, ModernBertModel
 
     torch.manual_seed(seed)
-    cfg = ModernBertConfig(vocab_size=512, hidden_size=128, intermediate_size=192, num_hidden_layers=3,
+    cfg = ModernBertConfig(vocab_size=512, hidden_size=128, intermediate_size=192, num_hidden_layers=layers,
                            num_attention_heads=2, local_attention=128, global_attn_every_n_layers=3,
                            max_position_embeddings=1024, pad_token_id=0)
     cfg._attn_implementation = "sdpa"
@@ -236,3 +236,137 @@ def test_qwen35_attention_caller_runs_b200(b200, gated):
         # same roundings; a sigmoid within an ulp of a bf16 rounding boundary may round the other way
         diff = (fused.view(fused.shape[0], -1).float() - y.float()).abs()
         assert (diff > 0).float().mean().item() < 0.01 and diff.max().item() <= 2e-2
+
+
+# --------------------------------------------------------------------------- training
+def _grads_of_interest(model):
+    """The output-proximate parameter gradients the reference's training test compares
+    (tests/test_varlen.py:250-268): the final norm and, in the last three layers, Wqkv, Wo, Wi, the
+    MLP's Wo and the MLP norm."""
+    picks = {"final_norm": model.final_norm.weight}
+    n = len(model.layers)
+    for li in (n - 1, n - 2, n - 3):
+        layer = model.layers[li]
+        picks[f"L{li}.attn.Wqkv"] = layer.attn.Wqkv.weight
+        picks[f"L{li}.attn.Wo"] = layer.attn.Wo.weight
+        picks[f"L{li}.mlp.Wi"] = layer.mlp.Wi.weight
+        picks[f"L{li}.mlp.Wo"] = layer.mlp.Wo.weight
+        picks[f"L{li}.mlp_norm"] = layer.mlp_norm.weight
+    return {name: p.grad.detach().float().clone() for name, p in picks.items()}
+
+
+def _train_step_grads(model, ids, am, seed):
+    """One forward + backward of the real tokens' outputs projected on a fixed random tensor. (The
+    reference's test squares the outputs, tests/test_varlen.py:271-282; after the final LayerNorm of
+    a random-init model that loss is almost constant, and its gradients are bf16 rounding noise.)"""
+    model.zero_grad(set_to_none=True)
+    out = model(input_ids=ids, attention_mask=am).last_hidden_state
+    loss = (out.float() * seed * am.unsqueeze(-1)).sum()
+    loss.backward()
+    return _grads_of_interest(model)
+
+
+def _grad_cos(a, b):
+    return F.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+
+
+def test_packed_training_step_on_b200_matches_sdpa_and_hf(b200, monkeypatch):
+    """A training step of a model packed with "b200" on a padded batch: the grad-enabled forward
+    takes the packed path (forward.py:634-657), each layer's attention runs this library's forward
+    kernel and its backward kernel (one backward call per layer), and the output-proximate
+    gradients are as close to stock HF run in fp32 (the same weights, upcast) as the reference's own
+    bf16 paths are (its SDPA backend and stock HF in bf16; the reference's test compares the packed
+    gradients with those two at cosine > 0.998, tests/test_varlen.py:304-348): no more than 0.002
+    below the closer of the two, and above 0.998 against the SDPA backend."""
+    from packed_encoders import forward
+    from packed_encoders_b200 import ops as b200_ops
+
+    stock = _tiny_modernbert(seed=5, layers=6)
+    on_b200, on_sdpa = copy.deepcopy(stock), copy.deepcopy(stock)
+    pe_ref.pack(on_b200, attention_backend="b200", validate=False)
+    pe_ref.pack(on_sdpa, attention_backend="sdpa", validate=False)
+    lengths = [40, 300, 7, 129, 220]
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    ids = torch.randint(1, 512, (len(lengths), max(lengths)), device="cuda", generator=gen)
+    am = torch.zeros_like(ids)
+    for i, n in enumerate(lengths):
+        am[i, :n] = 1
+    ids = ids * am
+    seed = torch.randn(*ids.shape, stock.config.hidden_size, device="cuda", generator=gen)
+
+    calls = {"varlen": 0, "backward": 0}
+    orig_varlen, orig_bwd = forward._varlen_forward, b200_ops.packed_attention_backward
+
+    def varlen_spy(*a, **k):
+        calls["varlen"] += 1
+        return orig_varlen(*a, **k)
+
+    def bwd_spy(*a, **k):
+        calls["backward"] += 1
+        return orig_bwd(*a, **k)
+
+    monkeypatch.setattr(forward, "_varlen_forward", varlen_spy)
+    monkeypatch.setattr(b200_ops, "packed_attention_backward", bwd_spy)
+    g_b200 = _train_step_grads(on_b200, ids, am, seed)
+    assert calls == {"varlen": 1, "backward": len(stock.layers)}
+    g_sdpa = _train_step_grads(on_sdpa, ids, am, seed)
+    g_hf = _train_step_grads(stock, ids, am, seed)
+    g_fp32 = _train_step_grads(copy.deepcopy(stock).float(), ids, am, seed)
+    cos = {name: tuple(round(_grad_cos(g[name], g_fp32[name]), 6) for g in (g_b200, g_sdpa, g_hf))
+           + (round(_grad_cos(g_b200[name], g_sdpa[name]), 6),) for name in g_b200}
+    print("packed training grads, cosine to fp32 HF of b200 / reference sdpa / HF bf16, and b200-vs-sdpa: "
+          f"{cos}")
+    for name, (c_b200, c_sdpa, c_hf, c_pair) in cos.items():
+        assert c_b200 >= max(c_sdpa, c_hf) - 0.002, f"{name}: b200 {c_b200:.5f} vs sdpa {c_sdpa:.5f} / HF {c_hf:.5f}"
+        assert c_pair > 0.998, f"{name}: b200 vs sdpa {c_pair:.5f}"
+
+
+def _flat_grads(weights):
+    return torch.cat([p.grad.float().flatten() for p in weights])
+
+
+def test_training_graph_on_b200_matches_eager_dense(b200):
+    """The reference's training-graph runner (train_graph.py:118-293) built with backend "b200":
+    the captured forward calls the rectangular b200 attention (each row one sequence, the window
+    per layer), the captured backward replays this library's backward kernels, and the gradients
+    match the eager dense SDPA forward it stands in for (the reference test's bars: cosine > 0.999,
+    relative L2 < 2e-2, tests/test_train_graph.py:122-142). pack(train_cuda_graph=True) routes the
+    grad-enabled forward through that runner."""
+    from packed_encoders import forward
+    from packed_encoders.config import ModernBertParams
+    from packed_encoders.state import get_state
+    from packed_encoders_b200 import ops as b200_ops
+
+    model = _tiny_modernbert(seed=6)
+    params = ModernBertParams.from_hf_config(model.config)
+    weights = [p for p in model.parameters() if p.requires_grad]
+    for p in weights:
+        p.grad = torch.zeros_like(p)
+    pe_ref.pack(model, attention_backend="b200", train_cuda_graph=True, cuda_graph_seq_cutoff=256, validate=False)
+    runner = get_state(model).train_graph_runner
+    assert runner is not None and runner._backend == "b200"
+    b, s = 8, 192
+    gen = torch.Generator(device="cuda").manual_seed(12)
+    ids = torch.randint(5, 512, (b, s), device="cuda", generator=gen)
+    mask = torch.ones((b, s), dtype=torch.long, device="cuda")
+    grad_seed = torch.randn((b, s, model.config.hidden_size), device="cuda", generator=gen, dtype=torch.bfloat16)
+
+    before = b200_ops.LAUNCHES["kernels"]
+    for p in weights:
+        p.grad.zero_()
+    out = model(input_ids=ids, attention_mask=mask).last_hidden_state
+    out.backward(grad_seed)
+    g_graph = _flat_grads(weights)
+    assert len(runner._cache) == 1 and b200_ops.LAUNCHES["kernels"] > before
+
+    p = forward.prologue(model, params, ids, mask, dense_mask=True, capture_safe=True)
+    ref = forward.core(model, params, p.x, p.cos_global, p.sin_global, p.cos_local, p.sin_local, p.full_mask,
+                       p.sliding_mask, backend="sdpa")
+    grads = torch.autograd.grad(ref, weights, grad_seed, allow_unused=True)
+    g_eager = torch.cat([(g if g is not None else torch.zeros_like(w)).float().flatten()
+                         for g, w in zip(grads, weights)])
+    cos = _grad_cos(g_graph, g_eager)
+    rel = ((g_graph - g_eager).norm() / (g_eager.norm() + 1e-9)).item()
+    fwd_cos = _grad_cos(out.detach().float(), ref.detach().float())
+    print(f"training graph on b200: forward cosine {fwd_cos:.6f}, grad cosine {cos:.6f}, grad rel L2 {rel:.4f}")
+    assert fwd_cos > 0.99 and cos > 0.999 and rel < 2e-2
