@@ -271,7 +271,7 @@ __global__ void clear_header_kernel(WsHeader* h) {
 //   TMA_OUT windowed-layer epilogue through one TMA store per warp; GATE output gate fused into
 //        the epilogue; STAGE epilogue rows staged through shared memory (head_dim 64).
 template <int D_, int BN_, int ST_, int VST_, int QB_, int NS_, int CPS_, int POLY_ = 0, int PASS_ = 0,
-          bool TMA_OUT_ = false, bool GATE_ = false, bool STAGE_ = true>
+          bool TMA_OUT_ = false, bool GATE_ = false, bool STAGE_ = true, bool QTM_ = false>
 struct Cfg {
   static constexpr bool kGate = GATE_;  // output gate fused into the epilogue (calls with a gate)
   static constexpr int D = D_, BN = BN_, ST = ST_, VST = VST_, QB = QB_, NS = NS_, CPS = CPS_, POLY = POLY_;
@@ -311,8 +311,13 @@ struct Cfg {
   static constexpr int kOffRows = kOffStage + kStageBytes;
   static constexpr int kSmemBytes = kOffRows + QB * kRowSlotBytes + 1024;  // + align slack
   static constexpr uint32_t kColO = NS * BN;
-  static constexpr uint32_t kTmemCols = (kColO + D <= 128) ? 128 : (kColO + D <= 256) ? 256 : 512;
-  static_assert(NS * BN <= (int)kColO && kColO + D <= kTmemCols, "TMEM budget");
+  // QTM: the unit's Q tile is copied into TMEM (tcgen05.cp, D / 2 columns after O) and the QK
+  // MMAs read it from there, so each of their k-steps reads only the K tile from shared memory.
+  static constexpr bool kQTmem = QTM_;
+  static constexpr uint32_t kColQ = kColO + D;
+  static constexpr uint32_t kTmemUsed = kColQ + (kQTmem ? D / 2 : 0);
+  static constexpr uint32_t kTmemCols = (kTmemUsed <= 128) ? 128 : (kTmemUsed <= 256) ? 256 : 512;
+  static_assert(NS * BN <= (int)kColO && kTmemUsed <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
   // CPS CTAs must fit one SM together: 228 KB of shared memory (1 KB of it reserved per CTA).
   static_assert((kSmemBytes + 1024) * CPS <= 228 * 1024, "shared memory of CPS CTAs per SM");
@@ -769,13 +774,17 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           uint32_t a_tm[4];
 #pragma unroll
           for (int k4 = 0; k4 < 4; ++k4) a_tm[k4] = tmem + C::col_s(sb) + (g * 4 + k4) * 8;
-          mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
+          if (g == C::BN / 64 - 1) {
+            // The last group carries the commits in the same elected block: one completion per unit
+            // (the epilogue waits on it, so it is committed first; with two S buffers the next
+            // unit's QK is issued before this P.V, so S-ready no longer implies earlier P.V
+            // completions), then the V stage release.
+            mma_ts4_commit_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u, o_full,
+                             last ? 1u : 0u, &v_empty[st]);
+          } else {
+            mma_ts4_w(tmem + C::kColO, a_tm, bdesc, idesc_pv, (g > 0 || !first) ? 1u : 0u);
+          }
         }
-        // One completion per unit (the epilogue waits on it, so it is committed first): with two
-        // S buffers the next unit's QK is issued before this P.V, so S-ready no longer implies
-        // earlier P.V completions.
-        if (last) mma_commit_w(o_full);
-        mma_commit_w(&v_empty[st]);
       };
       auto flush_one = [&]() {
         issue_pv(pend0, (int)(pfirst & 1u), (int)(plast & 1u));
@@ -797,6 +806,21 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         const int n_kv = reinterpret_cast<const int*>(smem + C::kOffRows + qb * C::kRowSlotBytes)[4];
         if (n_kv < 0) break;
         const uint32_t q_addr = smem_base + C::kOffQ + qb * C::kQBytes;
+        if constexpr (C::kQTmem) {
+          // Q -> TMEM, 16 columns of the head dim (128 rows x 32 bytes) per copy, read through the
+          // same descriptors the SS-form QK would use. Every MMA that read the previous unit's Q
+          // has completed: the P.V flush above waited for that unit's last P, which the softmax
+          // warps publish only after its S, the last QK's result, was ready. The copies are
+          // ordered before the QK MMAs that follow; their commit frees the shared-memory Q.
+#pragma unroll
+          for (int g = 0; g < C::kPanels; ++g) {
+            uint64_t qdesc[4];
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) qdesc[k4] = sw128_desc(q_addr + g * C::kQPanelBytes + k4 * 32, 16, 1024);
+            tc_cp4_w(tmem + C::kColQ + g * 32, qdesc);
+          }
+          mma_commit_w(&q_empty[qb]);
+        }
         for (int t = 0; t < n_kv; ++t, ++i) {
           const int st = (int)(i % C::ST);
           const int sb = (int)(i % C::NS);
@@ -814,11 +838,22 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
               adesc[k4] = sw128_desc(q_addr + g * C::kQPanelBytes + k4 * 32, 16, 1024);
               bdesc[k4] = sw128_desc(k_addr + g * C::kKVPanelBytes + k4 * 32, 16, 1024);
             }
-            mma_ss4_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, g > 0 ? 1u : 0u);
+            if constexpr (C::kQTmem) {
+              uint32_t a_tm[4];
+#pragma unroll
+              for (int k4 = 0; k4 < 4; ++k4) a_tm[k4] = tmem + C::kColQ + (g * 4 + k4) * 8;
+              if (g == C::D / 64 - 1)  // S ready, K stage free
+                mma_ts4_commit_w(tmem + C::col_s(sb), a_tm, bdesc, idesc_qk, g > 0 ? 1u : 0u, &s_full[sb], 1u,
+                                 &k_empty[st]);
+              else
+                mma_ts4_w(tmem + C::col_s(sb), a_tm, bdesc, idesc_qk, g > 0 ? 1u : 0u);
+            } else if (g == C::D / 64 - 1) {  // S ready, K stage free and, after the unit's last tile, Q free
+              mma_ss4_commit_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, g > 0 ? 1u : 0u, &s_full[sb],
+                               &k_empty[st], &q_empty[qb], t == n_kv - 1 ? 1u : 0u);
+            } else {
+              mma_ss4_w(tmem + C::col_s(sb), adesc, bdesc, idesc_qk, g > 0 ? 1u : 0u);
+            }
           }
-          mma_commit_w(&s_full[sb]);
-          mma_commit_w(&k_empty[st]);
-          if (t == n_kv - 1) mma_commit_w(&q_empty[qb]);
           if (npend == 0) pend0 = i;
           pfirst |= (t == 0 ? 1u : 0u) << npend;
           plast |= (t == n_kv - 1 ? 1u : 0u) << npend;
@@ -1609,9 +1644,9 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
   }
   if (p->gate) {  // output gate fused: separate instantiations, so ungated kernels carry no gate code
     switch (p->head_dim) {
-      case 64: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 0, false, true>>(p, s, info.sms);
+      case 64: return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 0, false, true, true, true>>(p, s, info.sms);
       case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4, 0, false, true>>(p, s, info.sms);
-      case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 0, false, true>>(p, s, info.sms);
+      case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 0, false, true, true, true>>(p, s, info.sms);
       default: return PE_B200_ERR_UNSUPPORTED;
     }
   }
@@ -1624,10 +1659,10 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
       if (windowed) return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2, 0, 0, true>>(p, s, info.sms);
       if (p->max_seqlen_k > 0 && p->max_seqlen_k <= kTileM)
         return launch_attention<Cfg<64, 64, 4, 3, 2, 3, 2>>(p, s, info.sms);
-      return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2>>(p, s, info.sms);
+      return launch_attention<Cfg<64, 64, 4, 3, 2, 2, 2, 0, 0, false, false, true, true>>(p, s, info.sms);
     }
     case 128: return launch_attention<Cfg<128, 128, 2, 2, 2, 2, 1, 4>>(p, s, info.sms);
-    case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0>>(p, s, info.sms);
+    case 256: return launch_attention<Cfg<256, 64, 3, 2, 1, 2, 1, 0, 0, false, false, true, true>>(p, s, info.sms);
     default: return PE_B200_ERR_UNSUPPORTED;
   }
 }

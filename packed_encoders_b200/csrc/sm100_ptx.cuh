@@ -283,6 +283,57 @@ __device__ __forceinline__ void mma_ts4_w(uint32_t d_tmem, const uint32_t (&a_tm
       "r"(a_tmem[0]), "r"(a_tmem[1]), "r"(a_tmem[2]), "r"(a_tmem[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]),
       "r"(accumulate), "r"(idesc));
 }
+// Four SS MMAs (as mma_ss4_w) followed by commits to `bar0`, `bar1` and, when `third` is
+// nonzero, `bar2`, all from one elected lane of one asm block.
+__device__ __forceinline__ void mma_ss4_commit_w(uint32_t d_tmem, const uint64_t (&a)[4], const uint64_t (&b)[4],
+                                                 uint32_t idesc, uint32_t accumulate, uint64_t* bar0,
+                                                 uint64_t* bar1, uint64_t* bar2, uint32_t third) {
+  asm volatile(
+      "{\n\t.reg .pred p, e, t, x;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 t, %9, %9;\n\tsetp.ne.and.b32 x, %14, 0, e;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %10, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %10, t;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%11];\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%12];\n\t"
+      "@x tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%13];\n\t}\n" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(accumulate),
+      "r"(idesc), "r"(smem_u32(bar0)), "r"(smem_u32(bar1)), "r"(smem_u32(bar2)), "r"(third)
+      : "memory");
+}
+// Four TS MMAs (as mma_ts4_w), then a commit to `first_bar` when `first` is nonzero and one to `bar`,
+// from one elected lane of one asm block.
+__device__ __forceinline__ void mma_ts4_commit_w(uint32_t d_tmem, const uint32_t (&a_tmem)[4],
+                                                 const uint64_t (&b)[4], uint32_t idesc, uint32_t accumulate,
+                                                 uint64_t* first_bar, uint32_t first, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred p, e, t, x;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 t, %9, %9;\n\tsetp.ne.and.b32 x, %12, 0, e;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %5, %10, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %6, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %10, t;\n\t"
+      "@x tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%11];\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%13];\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem[0]), "r"(a_tmem[1]), "r"(a_tmem[2]), "r"(a_tmem[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]),
+      "r"(accumulate), "r"(idesc), "r"(smem_u32(first_bar)), "r"(first), "r"(smem_u32(bar))
+      : "memory");
+}
+// Four shared-memory -> TMEM copies of 128 rows x 256 bits (16 bf16 of each row) from one elected
+// lane: copy j reads the matrix that descriptor d[j] describes and lands in TMEM columns
+// taddr + 8j .. +7, row r in lane r (the layout of an A operand read from TMEM).
+__device__ __forceinline__ void tc_cp4_w(uint32_t taddr, const uint64_t (&d)[4]) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 t1, t2, t3;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "add.u32 t1, %0, 8;\n\tadd.u32 t2, %0, 16;\n\tadd.u32 t3, %0, 24;\n\t"
+      "@e tcgen05.cp.cta_group::1.128x256b [%0], %1;\n\t"
+      "@e tcgen05.cp.cta_group::1.128x256b [t1], %2;\n\t"
+      "@e tcgen05.cp.cta_group::1.128x256b [t2], %3;\n\t"
+      "@e tcgen05.cp.cta_group::1.128x256b [t3], %4;\n\t}\n" ::"r"(taddr),
+      "l"(d[0]), "l"(d[1]), "l"(d[2]), "l"(d[3])
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
