@@ -18,6 +18,9 @@
 //   dV and dK accumulate in TMEM over the sub-blocks (lanes = keys), dQ goes to TMEM per sub-block
 //   and is added into an fp32 accumulator in global memory (vector atomics), scaled and converted
 //   by a last pass. TMEM: S 128 + dP 128 + dV 64 + dK 64 + dQ 64 = 448 columns (one CTA per SM).
+// Overlap: the P and dS tiles are double-buffered, and within a unit the MMA warp issues S and dP
+// of the NEXT sub-block before the dV, dK and dQ MMAs of this one, so the compute warps work on the
+// next sub-block's P and dS while the tensor core computes this one's gradients.
 // Roles (192 threads): warp 0 TMA producer (K, V per unit; Q, dO and a row slot per sub-block),
 // warp 1 MMA issuer, warps 2-5 one query row (or, for dK / dV, one key row) per thread.
 
@@ -49,10 +52,11 @@ constexpr int kOffK = 0;
 constexpr int kOffV = kOffK + kTileBytes;
 constexpr int kOffQ = kOffV + kTileBytes;                 // [kQST]
 constexpr int kOffDO = kOffQ + kQST * kTileBytes;         // [kQST]
-constexpr int kOffP = kOffDO + kQST * kTileBytes;         // 2 panels (keys 0-63, 64-127)
-constexpr int kOffDS = kOffP + 2 * kTileBytes;            // 2 panels
-constexpr int kSlotBytes = 64 + kTile * 8;                // header + per query row [klo, khi)
-constexpr int kOffSlot = kOffDS + 2 * kTileBytes;         // [kQST]
+constexpr int kPdsBytes = 2 * kTileBytes;                 // one P or dS tile: 2 panels (keys 0-63, 64-127)
+constexpr int kOffP = kOffDO + kQST * kTileBytes;         // [2] P tiles (sub-blocks alternate)
+constexpr int kOffDS = kOffP + 2 * kPdsBytes;             // [2] dS tiles
+constexpr int kSlotBytes = 64 + kTile * 4;                // header + per query row its key columns (2 x int16)
+constexpr int kOffSlot = kOffDS + 2 * kPdsBytes;          // [kQST]
 // barriers: kv_full kv_empty qd_full[2] qd_empty[2] row_empty[2] s_full p_ready dq_full dq_free
 //           dkv_full dkv_free
 constexpr int kNumBars = 2 + 3 * kQST + 6;
@@ -151,14 +155,14 @@ __device__ __forceinline__ BwdUnit bwd_unit(const BwdParams& p, const WorkItem& 
   return u;
 }
 
-// Row slot of one query sub-block: header, and per query row its allowed key interval [klo, khi)
-// in absolute tokens (its own sequence intersected with the band; empty past the valid rows).
+// Row slot of one query sub-block: header, and per query row its allowed key columns [lo, hi) of
+// the unit's key block (its own sequence intersected with the band; empty past the valid rows).
 // Rows of a run of short sequences find their sequence by counting boundaries (one coalesced load
 // per 32 boundaries and warp shuffles), as in the forward's row slots.
 __device__ __forceinline__ void bwd_write_slot(const BwdParams& p, const BwdUnit& u, int head, int step, int qt,
                                                uint8_t* slot_bytes, int lane) {
   int* hdr = reinterpret_cast<int*>(slot_bytes);
-  int2* rows = reinterpret_cast<int2*>(hdr + 16);
+  short2* rows = reinterpret_cast<short2*>(hdr + 16);
   const int nq = min(kTileM, u.q1 - qt);
   if (lane == 0) {
     hdr[kSlotQt] = qt;
@@ -193,7 +197,8 @@ __device__ __forceinline__ void bwd_write_slot(const BwdParams& p, const BwdUnit
       klo = cs + (p.window_left >= 0 ? max(0, pos - p.window_left) : 0);
       khi = cs + (p.window_right >= 0 ? min(len, pos + p.window_right + 1) : len);
     }
-    rows[r] = make_int2(klo, khi);
+    // as key columns of the unit's block, clamped to [0, 128] (an empty interval stays empty)
+    rows[r] = make_short2((short)min(max(klo - u.kb0, 0), bwd::kTile), (short)min(max(khi - u.kb0, 0), bwd::kTile));
   }
 }
 
@@ -296,22 +301,88 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     constexpr uint32_t idesc_kv = idesc_bf16_f32(kTile, 64, true, true);     // dV, dK: A, B MN-major
     constexpr uint32_t idesc_q = idesc_bf16_f32(kTile, 64, false, true);     // dQ: A K-major, B MN-major
     const uint32_t sb = smem_u32(smem);
-    uint32_t i = 0;
-    int nu = 0;
-    for (;; ++i) {
+    const uint32_t k_addr = sb + kOffK, v_addr = sb + kOffV;
+    int nu = 0;  // units whose K / V were waited for
+    int ug = 0;  // units whose gradient MMAs are all issued
+    // dV += P^T dO, dK += dS^T Q (A = the [query][key] tile read MN-major: M = keys in two 64-key
+    // panels, K = queries in 16-row steps of 2 KB; B = dO / Q read MN-major, N = head dim), then
+    // dQ = dS K (A = the dS tile K-major, B = the K tile MN-major) of sub-block j, whose P and dS
+    // are in tile buffer j % 2.
+    auto issue_grads = [&](uint32_t j, int jst, int jstep, int jsteps) {
+      const uint32_t pb = sb + kOffP + (j & 1) * kPdsBytes, db = sb + kOffDS + (j & 1) * kPdsBytes;
+      const uint32_t q_addr = sb + kOffQ + jst * kTileBytes, do_addr = sb + kOffDO + jst * kTileBytes;
+      if (jstep == 0 && ug > 0) {  // dV / dK accumulate afresh: the previous unit's were read out
+        mbar_wait(dkv_free, (ug - 1) & 1, p.err);
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        uint64_t a[4], b[4];
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = g * 4 + k4;
+          a[k4] = sw128_desc(pb + kk * 2048, kTileBytes, 1024);
+          b[k4] = sw128_desc(do_addr + kk * 2048, kTileBytes, 1024);
+        }
+        mma_ss4_w(tmem + kColDV, a, b, idesc_kv, (jstep > 0 || g > 0) ? 1u : 0u);
+      }
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        uint64_t a[4], b[4];
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = g * 4 + k4;
+          a[k4] = sw128_desc(db + kk * 2048, kTileBytes, 1024);
+          b[k4] = sw128_desc(q_addr + kk * 2048, kTileBytes, 1024);
+        }
+        if (g == 1)  // then Q and dO of this sub-block are no longer read
+          mma_ss4_commits_w(tmem + kColDK, a, b, idesc_kv, 1u, &qd_empty[jst], &qd_empty[jst], &qd_empty[jst], 1u);
+        else
+          mma_ss4_w(tmem + kColDK, a, b, idesc_kv, jstep > 0 ? 1u : 0u);
+      }
+      if (j > 0) mbar_wait(dq_free, (int)((j - 1) & 1), p.err);  // the previous dQ was read out
+      tc_fence_after();
+      const bool last = jstep == jsteps - 1;
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        uint64_t a[4], b[4];
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = g * 4 + k4;
+          a[k4] = sw128_desc(db + g * kTileBytes + k4 * 32, 16, 1024);
+          b[k4] = sw128_desc(k_addr + kk * 2048, kTileBytes, 1024);
+        }
+        if (g == 1)  // dQ ready; after the unit's last sub-block also dK / dV ready and K / V free
+          mma_ss4_commits_w(tmem + kColDQ, a, b, idesc_q, 1u, dq_full, dkv_full, kv_empty, last ? 7u : 1u);
+        else
+          mma_ss4_w(tmem + kColDQ, a, b, idesc_q, 0u);
+      }
+      if (last) ++ug;
+    };
+    // The sub-block whose gradient MMAs are not issued yet: within a unit they follow the next
+    // sub-block's S and dP. A unit's last sub-block is not held back: its gradients release K and V
+    // (kv_empty), which the producer waits for before it loads anything of the next unit, the next
+    // sub-block's Q and dO included.
+    bool pend = false;
+    uint32_t pi = 0;
+    int pst = 0, pstep = 0, psteps = 0;
+    for (uint32_t i = 0;; ++i) {
       const int st = (int)(i % kQST);
       mbar_wait(&qd_full[st], (int)(i / kQST) & 1, p.err);
       tc_fence_after();
       const int* hdr = reinterpret_cast<const int*>(smem + kOffSlot + st * kSlotBytes);
       const int step = hdr[kSlotStep], steps = hdr[kSlotSteps];
       if (steps < 0) break;
-      if (step == 0) {
-        mbar_wait(kv_full, nu & 1, p.err);
-        if (nu > 0) mbar_wait(dkv_free, (nu - 1) & 1, p.err);  // the previous unit's dK / dV were read
+      if (pend) {  // S and dP of the pending sub-block were read out; its P and dS are written
+        mbar_wait(p_ready, (int)(pi & 1), p.err);
         tc_fence_after();
       }
+      if (step == 0) {  // nothing is pending here: the previous unit's last gradients were issued
+        mbar_wait(kv_full, nu & 1, p.err);
+        tc_fence_after();
+        ++nu;
+      }
       const uint32_t q_addr = sb + kOffQ + st * kTileBytes, do_addr = sb + kOffDO + st * kTileBytes;
-      const uint32_t k_addr = sb + kOffK, v_addr = sb + kOffV;
       {  // S = Q K^T, dP = dO V^T (K-major operands, four 16-deep steps over the head dim)
         uint64_t a[4], b[4];
 #pragma unroll
@@ -325,57 +396,20 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           a[k4] = sw128_desc(do_addr + k4 * 32, 16, 1024);
           b[k4] = sw128_desc(v_addr + k4 * 32, 16, 1024);
         }
-        mma_ss4_w(tmem + kColDP, a, b, idesc_s, 0u);
-        mma_commit_w(s_full);
+        mma_ss4_commits_w(tmem + kColDP, a, b, idesc_s, 0u, s_full, s_full, s_full, 1u);
       }
-      mbar_wait(p_ready, (int)(i & 1), p.err);
-      tc_fence_after();
-      // dV += P^T dO, dK += dS^T Q: A = the [query][key] tile read MN-major (M = keys in two
-      // 64-key panels 16 KB apart), B = dO / Q read MN-major (N = head dim), K = queries in
-      // 16-row steps of 2 KB.
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        uint64_t a[4], b[4];
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const int kk = g * 4 + k4;
-          a[k4] = sw128_desc(sb + kOffP + kk * 2048, kTileBytes, 1024);
-          b[k4] = sw128_desc(do_addr + kk * 2048, kTileBytes, 1024);
-        }
-        mma_ss4_w(tmem + kColDV, a, b, idesc_kv, (step > 0 || g > 0) ? 1u : 0u);
-      }
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        uint64_t a[4], b[4];
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const int kk = g * 4 + k4;
-          a[k4] = sw128_desc(sb + kOffDS + kk * 2048, kTileBytes, 1024);
-          b[k4] = sw128_desc(q_addr + kk * 2048, kTileBytes, 1024);
-        }
-        mma_ss4_w(tmem + kColDK, a, b, idesc_kv, (step > 0 || g > 0) ? 1u : 0u);
-      }
-      mma_commit_w(&qd_empty[st]);  // Q and dO of this sub-block are no longer read
-      // dQ = dS K: A = the dS tile K-major (K = keys: 32-byte steps inside a panel, two panels),
-      // B = the K tile MN-major (K = keys in 16-row steps, N = head dim).
-      if (i > 0) mbar_wait(dq_free, (int)((i - 1) & 1), p.err);
-      tc_fence_after();
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        uint64_t a[4], b[4];
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const int kk = g * 4 + k4;
-          a[k4] = sw128_desc(sb + kOffDS + g * kTileBytes + k4 * 32, 16, 1024);
-          b[k4] = sw128_desc(k_addr + kk * 2048, kTileBytes, 1024);
-        }
-        mma_ss4_w(tmem + kColDQ, a, b, idesc_q, g > 0 ? 1u : 0u);
-      }
-      mma_commit_w(dq_full);
-      if (step == steps - 1) {
-        mma_commit_w(dkv_full);
-        mma_commit_w(kv_empty);
-        ++nu;
+      if (pend) issue_grads(pi, pst, pstep, psteps);
+      if (step == steps - 1) {  // the unit's last sub-block: its gradients now
+        mbar_wait(p_ready, (int)(i & 1), p.err);
+        tc_fence_after();
+        issue_grads(i, st, step, steps);
+        pend = false;
+      } else {
+        pend = true;
+        pi = i;
+        pst = st;
+        pstep = step;
+        psteps = steps;
       }
     }
   } else {
@@ -383,26 +417,86 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane: query row (S, dP, dQ) or key row (dK, dV)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    uint8_t* p_row = smem + kOffP + r * 128;
-    uint8_t* ds_row = smem + kOffDS + r * 128;
     const float c2 = p.scale_log2;
-    uint32_t i = 0;
-    int nu = 0;  // units finished
-    for (;; ++i) {
+    int ug = 0;  // units whose dK / dV were read out
+    // dQ of sub-block j out of TMEM and into the fp32 accumulator; after a unit's last sub-block,
+    // that unit's dK and dV (TMEM lane r is key row r there) out to dk / dv.
+    auto finish = [&](uint32_t j, int qt, int nq, int head, bool last, int kb0, int nk) {
+      mbar_wait(dq_full, (int)(j & 1), p.err);
+      tc_fence_after();
+      uint32_t dq[2][32];
+      tmem_ld32(tmem + lane_base + kColDQ, dq[0]);
+      tmem_ld32(tmem + lane_base + kColDQ + 32, dq[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      if (r < nq && qt + r < p.total) {
+        float* dst = p.dq_acc + ((long long)(qt + r) * p.heads + head) * 64;
+#pragma unroll
+        for (int c4 = 0; c4 < 16; ++c4) {
+          const uint32_t* w = &dq[c4 >> 3][(c4 & 7) * 4];
+          red_add_v4(dst + 4 * c4, __uint_as_float(w[0]), __uint_as_float(w[1]), __uint_as_float(w[2]),
+                     __uint_as_float(w[3]));
+        }
+      }
+      if (!last) return;
+      mbar_wait(dkv_full, ug & 1, p.err);
+      tc_fence_after();
+      uint32_t dvr[2][32], dkr[2][32];
+      tmem_ld32(tmem + lane_base + kColDV, dvr[0]);
+      tmem_ld32(tmem + lane_base + kColDV + 32, dvr[1]);
+      tmem_ld32(tmem + lane_base + kColDK, dkr[0]);
+      tmem_ld32(tmem + lane_base + kColDK + 32, dkr[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dkv_free);
+      ++ug;
+      if (r < nk && kb0 + r < p.total) {
+        uint4* dvp = reinterpret_cast<uint4*>(p.dv + (long long)(kb0 + r) * p.dv_tok + (long long)head * p.dv_head);
+        uint4* dkp = reinterpret_cast<uint4*>(p.dk + (long long)(kb0 + r) * p.dk_tok + (long long)head * p.dk_head);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const uint32_t* v = &dvr[c8 >> 2][(c8 & 3) * 8];
+          const uint32_t* k = &dkr[c8 >> 2][(c8 & 3) * 8];
+          dvp[c8] = make_uint4(pack_bf16x2(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                               pack_bf16x2(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                               pack_bf16x2(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                               pack_bf16x2(__uint_as_float(v[6]), __uint_as_float(v[7])));
+          const float sc = p.scale;
+          dkp[c8] = make_uint4(pack_bf16x2(__uint_as_float(k[0]) * sc, __uint_as_float(k[1]) * sc),
+                               pack_bf16x2(__uint_as_float(k[2]) * sc, __uint_as_float(k[3]) * sc),
+                               pack_bf16x2(__uint_as_float(k[4]) * sc, __uint_as_float(k[5]) * sc),
+                               pack_bf16x2(__uint_as_float(k[6]) * sc, __uint_as_float(k[7]) * sc));
+        }
+      }
+    };
+    // The previous sub-block, whose dQ (and dK / dV) are read out after this one's P and dS are
+    // written: its gradient MMAs run on the tensor core meanwhile.
+    bool pend = false;
+    uint32_t pi = 0;
+    int pqt = 0, pnq = 0, phead = 0, pkb0 = 0, pnk = 0;
+    bool plast = false;
+    for (uint32_t i = 0;; ++i) {
       const int st = (int)(i % kQST);
       mbar_wait(&qd_full[st], (int)(i / kQST) & 1, p.err);
       const int* hdr = reinterpret_cast<const int*>(smem + kOffSlot + st * kSlotBytes);
       const int qt = hdr[kSlotQt], nq = hdr[kSlotNq], kb0 = hdr[kSlotKb], nk = hdr[kSlotNk];
       const int head = hdr[kSlotHead], step = hdr[kSlotStep], steps = hdr[kSlotSteps];
       if (steps < 0) break;
-      const int2 kr = reinterpret_cast<const int2*>(hdr + 16)[r];
+      const short2 kr = reinterpret_cast<const short2*>(hdr + 16)[r];
       __syncwarp();
       if (lane == 0) mbar_arrive(&row_empty[st]);
       const bool row_valid = r < nq;
       const long long hrow = (long long)head * p.total + qt + r;
       const float lse2 = row_valid ? p.lse2[hrow] : 0.f;
       const float dsum = row_valid ? p.dsum[hrow] : 0.f;
-      const int c_lo = kr.x - kb0, c_hi = kr.y - kb0;  // my allowed key columns
+      const int c_lo = kr.x, c_hi = kr.y;  // my allowed key columns
+      // This tile buffer was last read by the gradient MMAs of sub-block i - 2, complete since
+      // finish(i - 2) waited for their dQ.
+      uint8_t* p_row = smem + kOffP + (i & 1) * kPdsBytes + r * 128;
+      uint8_t* ds_row = smem + kOffDS + (i & 1) * kPdsBytes + r * 128;
       mbar_wait(s_full, (int)(i & 1), p.err);
       tc_fence_after();
 #pragma unroll 1
@@ -437,58 +531,17 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
-      // dQ of this sub-block: out of TMEM, then added into the fp32 accumulator.
-      mbar_wait(dq_full, (int)(i & 1), p.err);
-      tc_fence_after();
-      uint32_t dq[2][32];
-      tmem_ld32(tmem + lane_base + kColDQ, dq[0]);
-      tmem_ld32(tmem + lane_base + kColDQ + 32, dq[1]);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
-      if (row_valid && qt + r < p.total) {
-        float* dst = p.dq_acc + ((long long)(qt + r) * p.heads + head) * 64;
-#pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4) {
-          const uint32_t* w = &dq[c4 >> 3][(c4 & 7) * 4];
-          red_add_v4(dst + 4 * c4, __uint_as_float(w[0]), __uint_as_float(w[1]), __uint_as_float(w[2]),
-                     __uint_as_float(w[3]));
-        }
-      }
-      if (step == steps - 1) {  // the unit's dK and dV: TMEM lane r is key row r here
-        mbar_wait(dkv_full, nu & 1, p.err);
-        tc_fence_after();
-        uint32_t dvr[2][32], dkr[2][32];
-        tmem_ld32(tmem + lane_base + kColDV, dvr[0]);
-        tmem_ld32(tmem + lane_base + kColDV + 32, dvr[1]);
-        tmem_ld32(tmem + lane_base + kColDK, dkr[0]);
-        tmem_ld32(tmem + lane_base + kColDK + 32, dkr[1]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dkv_free);
-        ++nu;
-        if (r < nk && kb0 + r < p.total) {
-          uint4* dvp = reinterpret_cast<uint4*>(p.dv + (long long)(kb0 + r) * p.dv_tok + (long long)head * p.dv_head);
-          uint4* dkp = reinterpret_cast<uint4*>(p.dk + (long long)(kb0 + r) * p.dk_tok + (long long)head * p.dk_head);
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            const uint32_t* v = &dvr[c8 >> 2][(c8 & 3) * 8];
-            const uint32_t* k = &dkr[c8 >> 2][(c8 & 3) * 8];
-            dvp[c8] = make_uint4(pack_bf16x2(__uint_as_float(v[0]), __uint_as_float(v[1])),
-                                 pack_bf16x2(__uint_as_float(v[2]), __uint_as_float(v[3])),
-                                 pack_bf16x2(__uint_as_float(v[4]), __uint_as_float(v[5])),
-                                 pack_bf16x2(__uint_as_float(v[6]), __uint_as_float(v[7])));
-            const float sc = p.scale;
-            dkp[c8] = make_uint4(pack_bf16x2(__uint_as_float(k[0]) * sc, __uint_as_float(k[1]) * sc),
-                                 pack_bf16x2(__uint_as_float(k[2]) * sc, __uint_as_float(k[3]) * sc),
-                                 pack_bf16x2(__uint_as_float(k[4]) * sc, __uint_as_float(k[5]) * sc),
-                                 pack_bf16x2(__uint_as_float(k[6]) * sc, __uint_as_float(k[7]) * sc));
-          }
-        }
-      }
+      if (pend) finish(pi, pqt, pnq, phead, plast, pkb0, pnk);
+      pend = true;
+      pi = i;
+      pqt = qt;
+      pnq = nq;
+      phead = head;
+      plast = step == steps - 1;
+      pkb0 = kb0;
+      pnk = nk;
     }
+    if (pend) finish(pi, pqt, pnq, phead, plast, pkb0, pnk);
   }
 
   tc_fence_before();

@@ -334,6 +334,28 @@ __device__ __forceinline__ void tc_cp4_w(uint32_t taddr, const uint64_t (&d)[4])
       "l"(d[0]), "l"(d[1]), "l"(d[2]), "l"(d[3])
       : "memory");
 }
+// Four SS MMAs (as mma_ss4_w), then commits to those of `bar0`, `bar1`, `bar2` whose bit is set in
+// `mask` (bit 0 = bar0), from one elected lane of one asm block.
+__device__ __forceinline__ void mma_ss4_commits_w(uint32_t d_tmem, const uint64_t (&a)[4], const uint64_t (&b)[4],
+                                                  uint32_t idesc, uint32_t accumulate, uint64_t* bar0,
+                                                  uint64_t* bar1, uint64_t* bar2, uint32_t mask) {
+  asm volatile(
+      "{\n\t.reg .pred p, e, t, x0, x1, x2;\n\t.reg .b32 m;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %9, 0;\n\tsetp.eq.b32 t, %9, %9;\n\t"
+      "and.b32 m, %14, 1;\n\tsetp.ne.and.b32 x0, m, 0, e;\n\t"
+      "and.b32 m, %14, 2;\n\tsetp.ne.and.b32 x1, m, 0, e;\n\t"
+      "and.b32 m, %14, 4;\n\tsetp.ne.and.b32 x2, m, 0, e;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %10, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %10, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %10, t;\n\t"
+      "@x0 tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%11];\n\t"
+      "@x1 tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%12];\n\t"
+      "@x2 tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%13];\n\t}\n" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(accumulate),
+      "r"(idesc), "r"(smem_u32(bar0)), "r"(smem_u32(bar1)), "r"(smem_u32(bar2)), "r"(mask)
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"

@@ -68,6 +68,9 @@ CASES = [
     ([17, 250, 9, 0, 128], 2, (16, 3), False),
     ([30] * 40 + [5, 100], 3, (-1, -1), False),
     ([2000, 40], 2, (-1, -1), False),
+    # more units (key block, head) than SMs: every CTA runs several units back to back
+    ([300, 45, 260, 700, 130] * 12, 8, (-1, -1), False),
+    ([300, 45, 260, 700, 130] * 12, 8, (64, 64), False),
 ]
 
 
