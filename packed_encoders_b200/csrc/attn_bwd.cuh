@@ -21,8 +21,10 @@
 // Overlap: the P and dS tiles are double-buffered, and within a unit the MMA warp issues S and dP
 // of the NEXT sub-block before the dV, dK and dQ MMAs of this one, so the compute warps work on the
 // next sub-block's P and dS while the tensor core computes this one's gradients.
-// Roles (192 threads): warp 0 TMA producer (K, V per unit; Q, dO and a row slot per sub-block),
-// warp 1 MMA issuer, warps 2-5 one query row (or, for dK / dV, one key row) per thread.
+// Roles (320 threads): warp 0 TMA producer (K, V per unit; Q, dO and a row slot per sub-block),
+// warp 1 MMA issuer, warps 2-9 compute: one query row (or, for dK / dV, one key row) per thread and
+// half of its columns (warps 2-5 keys 0-63 and dQ columns 0-31 and dV; warps 6-9 keys 64-127, dQ
+// columns 32-63 and dK), so two compute warps share each SM sub-partition.
 
 struct BwdParams {
   const int32_t* cu;
@@ -65,7 +67,8 @@ constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;      // + align slack
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
 constexpr uint32_t kTmemCols = 512;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kComputeWarps = 8;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 }  // namespace bwd
 
@@ -216,11 +219,11 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   uint64_t* qd_empty = qd_full + kQST;       // [kQST]
   uint64_t* row_empty = qd_empty + kQST;     // [kQST]
   uint64_t* s_full = row_empty + kQST;       // S and dP of the sub-block are in TMEM
-  uint64_t* p_ready = s_full + 1;            // P and dS are in shared memory (4 warps)
+  uint64_t* p_ready = s_full + 1;            // P and dS are in shared memory (8 warps)
   uint64_t* dq_full = p_ready + 1;           // dQ of the sub-block is in TMEM (all its MMAs done)
-  uint64_t* dq_free = dq_full + 1;           // dQ was read out of TMEM (4 warps)
+  uint64_t* dq_free = dq_full + 1;           // dQ was read out of TMEM (8 warps)
   uint64_t* dkv_full = dq_free + 1;          // the unit's dK and dV are complete
-  uint64_t* dkv_free = dkv_full + 1;         // dK and dV were read out of TMEM (4 warps)
+  uint64_t* dkv_free = dkv_full + 1;         // dK and dV were read out of TMEM (8 warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -229,14 +232,14 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     for (int i = 0; i < kQST; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
-      mbar_init(&row_empty[i], 4);
+      mbar_init(&row_empty[i], kComputeWarps);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_ready, 4);
+    mbar_init(p_ready, kComputeWarps);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 4);
+    mbar_init(dq_free, kComputeWarps);
     mbar_init(dkv_full, 1);
-    mbar_init(dkv_free, 4);
+    mbar_init(dkv_free, kComputeWarps);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -415,6 +418,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   } else {
     // ------------------------------------------------------------------ P, dS, dQ, dK, dV rows
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;   // 0: keys 0-63 (panel 0), dQ columns 0-31, dV; 1: keys 64-127, dQ 32-63, dK
     const int r = quarter * 32 + lane;  // TMEM lane: query row (S, dP, dQ) or key row (dK, dV)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float c2 = p.scale_log2;
@@ -424,51 +428,41 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     auto finish = [&](uint32_t j, int qt, int nq, int head, bool last, int kb0, int nk) {
       mbar_wait(dq_full, (int)(j & 1), p.err);
       tc_fence_after();
-      uint32_t dq[2][32];
-      tmem_ld32(tmem + lane_base + kColDQ, dq[0]);
-      tmem_ld32(tmem + lane_base + kColDQ + 32, dq[1]);
+      uint32_t dq[32];  // my half of the row's 64 dQ columns
+      tmem_ld32(tmem + lane_base + kColDQ + half * 32, dq);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
       if (r < nq && qt + r < p.total) {
-        float* dst = p.dq_acc + ((long long)(qt + r) * p.heads + head) * 64;
+        float* dst = p.dq_acc + ((long long)(qt + r) * p.heads + head) * 64 + half * 32;
 #pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4) {
-          const uint32_t* w = &dq[c4 >> 3][(c4 & 7) * 4];
-          red_add_v4(dst + 4 * c4, __uint_as_float(w[0]), __uint_as_float(w[1]), __uint_as_float(w[2]),
-                     __uint_as_float(w[3]));
-        }
+        for (int c4 = 0; c4 < 8; ++c4)
+          red_add_v4(dst + 4 * c4, __uint_as_float(dq[4 * c4]), __uint_as_float(dq[4 * c4 + 1]),
+                     __uint_as_float(dq[4 * c4 + 2]), __uint_as_float(dq[4 * c4 + 3]));
       }
       if (!last) return;
       mbar_wait(dkv_full, ug & 1, p.err);
       tc_fence_after();
-      uint32_t dvr[2][32], dkr[2][32];
-      tmem_ld32(tmem + lane_base + kColDV, dvr[0]);
-      tmem_ld32(tmem + lane_base + kColDV + 32, dvr[1]);
-      tmem_ld32(tmem + lane_base + kColDK, dkr[0]);
-      tmem_ld32(tmem + lane_base + kColDK + 32, dkr[1]);
+      uint32_t g[2][32];  // dV (half 0) or dK (half 1) of key row r
+      tmem_ld32(tmem + lane_base + (half ? kColDK : kColDV), g[0]);
+      tmem_ld32(tmem + lane_base + (half ? kColDK : kColDV) + 32, g[1]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dkv_free);
       ++ug;
       if (r < nk && kb0 + r < p.total) {
-        uint4* dvp = reinterpret_cast<uint4*>(p.dv + (long long)(kb0 + r) * p.dv_tok + (long long)head * p.dv_head);
-        uint4* dkp = reinterpret_cast<uint4*>(p.dk + (long long)(kb0 + r) * p.dk_tok + (long long)head * p.dk_head);
+        uint4* dst = half ? reinterpret_cast<uint4*>(p.dk + (long long)(kb0 + r) * p.dk_tok + (long long)head * p.dk_head)
+                          : reinterpret_cast<uint4*>(p.dv + (long long)(kb0 + r) * p.dv_tok + (long long)head * p.dv_head);
+        const float sc = half ? p.scale : 1.f;  // dK = scale * dS^T Q
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
-          const uint32_t* v = &dvr[c8 >> 2][(c8 & 3) * 8];
-          const uint32_t* k = &dkr[c8 >> 2][(c8 & 3) * 8];
-          dvp[c8] = make_uint4(pack_bf16x2(__uint_as_float(v[0]), __uint_as_float(v[1])),
-                               pack_bf16x2(__uint_as_float(v[2]), __uint_as_float(v[3])),
-                               pack_bf16x2(__uint_as_float(v[4]), __uint_as_float(v[5])),
-                               pack_bf16x2(__uint_as_float(v[6]), __uint_as_float(v[7])));
-          const float sc = p.scale;
-          dkp[c8] = make_uint4(pack_bf16x2(__uint_as_float(k[0]) * sc, __uint_as_float(k[1]) * sc),
-                               pack_bf16x2(__uint_as_float(k[2]) * sc, __uint_as_float(k[3]) * sc),
-                               pack_bf16x2(__uint_as_float(k[4]) * sc, __uint_as_float(k[5]) * sc),
-                               pack_bf16x2(__uint_as_float(k[6]) * sc, __uint_as_float(k[7]) * sc));
+          const uint32_t* v = &g[c8 >> 2][(c8 & 3) * 8];
+          dst[c8] = make_uint4(pack_bf16x2(__uint_as_float(v[0]) * sc, __uint_as_float(v[1]) * sc),
+                               pack_bf16x2(__uint_as_float(v[2]) * sc, __uint_as_float(v[3]) * sc),
+                               pack_bf16x2(__uint_as_float(v[4]) * sc, __uint_as_float(v[5]) * sc),
+                               pack_bf16x2(__uint_as_float(v[6]) * sc, __uint_as_float(v[7]) * sc));
         }
       }
     };
@@ -478,6 +472,10 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     uint32_t pi = 0;
     int pqt = 0, pnq = 0, phead = 0, pkb0 = 0, pnk = 0;
     bool plast = false;
+    // Within a unit the next sub-block starts 128 query rows further on: its rows' LSE and
+    // rowsum(dO * O) are loaded while this sub-block's dQ is read out.
+    bool have_next = false;
+    float next_lse2 = 0.f, next_dsum = 0.f;
     for (uint32_t i = 0;; ++i) {
       const int st = (int)(i % kQST);
       mbar_wait(&qd_full[st], (int)(i / kQST) & 1, p.err);
@@ -490,8 +488,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       if (lane == 0) mbar_arrive(&row_empty[st]);
       const bool row_valid = r < nq;
       const long long hrow = (long long)head * p.total + qt + r;
-      const float lse2 = row_valid ? p.lse2[hrow] : 0.f;
-      const float dsum = row_valid ? p.dsum[hrow] : 0.f;
+      const float lse2 = row_valid ? (have_next ? next_lse2 : p.lse2[hrow]) : 0.f;
+      const float dsum = row_valid ? (have_next ? next_dsum : p.dsum[hrow]) : 0.f;
       const int c_lo = kr.x, c_hi = kr.y;  // my allowed key columns
       // This tile buffer was last read by the gradient MMAs of sub-block i - 2, complete since
       // finish(i - 2) waited for their dQ.
@@ -500,7 +498,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       mbar_wait(s_full, (int)(i & 1), p.err);
       tc_fence_after();
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {  // 32 keys at a time
+      for (int cc = 2 * half; cc < 2 * half + 2; ++cc) {  // 32 keys at a time, my half of the keys
         uint32_t s[32], dp[32];
         tmem_ld32(tmem + lane_base + kColS + cc * 32, s);
         tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
@@ -531,6 +529,12 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
+      have_next = step < steps - 1;
+      if (have_next) {
+        const bool ok = qt + kTileM + r < p.total;
+        next_lse2 = ok ? p.lse2[hrow + kTileM] : 0.f;
+        next_dsum = ok ? p.dsum[hrow + kTileM] : 0.f;
+      }
       if (pend) finish(pi, pqt, pnq, phead, plast, pkb0, pnk);
       pend = true;
       pi = i;
