@@ -16,8 +16,9 @@
 //   128B-swizzled [query][key] tile in shared memory, which is both the MN-major A operand of
 //   dV += P^T dO and dK += dS^T Q (M = 128 keys) and the K-major A operand of dQ = dS K;
 //   dV and dK accumulate in TMEM over the sub-blocks (lanes = keys), dQ goes to TMEM per sub-block
-//   and is added into an fp32 accumulator in global memory (vector atomics), scaled and converted
-//   by a last pass. TMEM: S 128 + dP 128 + dV 64 + dK 64 + dQ 64 = 448 columns (one CTA per SM).
+//   and is added into an fp32 accumulator in global memory (vector reductions of whole 128-byte
+//   lines, through the sub-block's dS tile, free once dQ is computed), then scaled and converted by
+//   a last pass. TMEM: S 128 + dP 128 + dV 64 + dK 64 + dQ 64 = 448 columns (one CTA per SM).
 // Overlap: the P and dS tiles are double-buffered, and within a unit the MMA warp issues S and dP
 // of the NEXT sub-block before the dV, dK and dQ MMAs of this one, so the compute warps work on the
 // next sub-block's P and dS while the tensor core computes this one's gradients.
@@ -434,12 +435,29 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      if (r < nq && qt + r < p.total) {
-        float* dst = p.dq_acc + ((long long)(qt + r) * p.heads + head) * 64 + half * 32;
+      // Add my half-row (32 fp32) into the accumulator with whole 128-byte lines per row: the warp
+      // stages its 32 rows in its own rows of sub-block j's dS panel (its dK and dQ MMAs are
+      // complete), 128B-swizzled (chunk c of row r at r * 128 + (c ^ r % 8) * 16, so the 32 lanes of
+      // a store cover all banks), and reads them back eight lanes per row: each vector reduction
+      // then covers four rows' full lines instead of 16 bytes of 32 rows.
+      {
+        uint8_t* stage = smem + kOffDS + (j & 1) * kPdsBytes + half * kTileBytes;
+        uint8_t* row = stage + r * 128;
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4)
-          red_add_v4(dst + 4 * c4, __uint_as_float(dq[4 * c4]), __uint_as_float(dq[4 * c4 + 1]),
-                     __uint_as_float(dq[4 * c4 + 2]), __uint_as_float(dq[4 * c4 + 3]));
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
+              make_uint4(dq[4 * c], dq[4 * c + 1], dq[4 * c + 2], dq[4 * c + 3]);
+        __syncwarp();
+        const int c = lane & 7;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int rr = quarter * 32 + 4 * k + (lane >> 3);
+          const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+          if (rr < nq && qt + rr < p.total)
+            red_add_v4(p.dq_acc + ((long long)(qt + rr) * p.heads + head) * 64 + half * 32 + 4 * c,
+                       __uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z), __uint_as_float(w.w));
+        }
+        __syncwarp();
       }
       if (!last) return;
       mbar_wait(dkv_full, ug & 1, p.err);
@@ -498,7 +516,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       mbar_wait(s_full, (int)(i & 1), p.err);
       tc_fence_after();
 #pragma unroll 1
-      for (int cc = 2 * half; cc < 2 * half + 2; ++cc) {  // 32 keys at a time, my half of the keys
+      for (int h2 = 0; h2 < 2; ++h2) {  // my 64 keys, 32 at a time
+        const int cc = 2 * half + h2;   // 32-key chunk of the 128 keys
         uint32_t s[32], dp[32];
         tmem_ld32(tmem + lane_base + kColS + cc * 32, s);
         tmem_ld32(tmem + lane_base + kColDP + cc * 32, dp);
@@ -514,14 +533,13 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           pk[j] = pack_bf16x2(p0, p1);
           dk16[j] = pack_bf16x2(p0 * (__uint_as_float(dp[2 * j]) - dsum), p1 * (__uint_as_float(dp[2 * j + 1]) - dsum));
         }
-        // chunks 4*(cc % 2) .. +3 of panel cc / 2, swizzled by the row
-        const int panel = (cc >> 1) * kTileBytes;
+        // chunks 4*h2 .. +3 of panel `half`, swizzled by the row
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          const int ch = ((cc & 1) * 4 + q4) ^ (r & 7);
-          *reinterpret_cast<uint4*>(p_row + panel + (ch << 4)) =
+          const int ch = (h2 * 4 + q4) ^ (r & 7);
+          *reinterpret_cast<uint4*>(p_row + half * kTileBytes + (ch << 4)) =
               make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-          *reinterpret_cast<uint4*>(ds_row + panel + (ch << 4)) =
+          *reinterpret_cast<uint4*>(ds_row + half * kTileBytes + (ch << 4)) =
               make_uint4(dk16[4 * q4], dk16[4 * q4 + 1], dk16[4 * q4 + 2], dk16[4 * q4 + 3]);
         }
       }
