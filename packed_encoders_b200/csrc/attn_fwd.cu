@@ -876,24 +876,32 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
     const float NEG_INF = -__int_as_float(0x7f800000);
     const float c2 = p.scale_log2;
     uint32_t i = 0;
-    int lu = 0;
-    for (;; ++lu) {
-      // The unit's header and this row's allowed keys [klo, khi) come from the producer's row
-      // slot, published with the unit's Q tile.
-      const int qb = lu % C::QB;
-      mbar_wait(&q_full[qb], (lu / C::QB) & 1, p.err);
+    // A unit's header and this row's allowed keys [klo, khi) come from the producer's row slot,
+    // published with the unit's Q tile (a negative key-tile count ends the stream). The next
+    // unit's header is read while this unit's last P.V is still running (before the epilogue's
+    // wait for it): neither waits for the other, since the producer publishes a unit's slot
+    // without waiting for any epilogue.
+    UnitInfo ui;
+    int klo = 0, khi = 0;
+    auto read_header = [&](int u, UnitInfo& h, int& lo, int& hi) {
+      const int qb = u % C::QB;
+      mbar_wait(&q_full[qb], (u / C::QB) & 1, p.err);
       const int* slot = reinterpret_cast<const int*>(smem + C::kOffRows + qb * C::kRowSlotBytes);
-      UnitInfo ui;
-      ui.q_row0 = slot[0];
-      ui.nq = slot[1];
-      ui.head = slot[2];
-      ui.kv_lo = slot[3];
-      ui.n_kv = slot[4];
-      if (ui.n_kv < 0) break;
+      h.q_row0 = slot[0];
+      h.nq = slot[1];
+      h.head = slot[2];
+      h.kv_lo = slot[3];
+      h.n_kv = slot[4];
+      if (h.n_kv < 0) return;
       const int2 kr = reinterpret_cast<const int2*>(slot + 16)[r];
-      const int klo = kr.x, khi = kr.y;
+      lo = kr.x;
+      hi = kr.y;
       __syncwarp();
       if (lane == 0) mbar_arrive(&row_empty[qb]);
+    };
+    read_header(0, ui, klo, khi);
+    for (int lu = 0;; ++lu) {
+      if (ui.n_kv < 0) break;
       const bool row_valid = r < ui.nq;
       const int tq = ui.q_row0 + r;
       float m_run = NEG_INF, l_run = 0.f;
@@ -1048,6 +1056,9 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           for (int j = 0; j < kGateChunk; ++j) g_next[j] = load_gate8(p, tq, ui.head, j * 8);
         }
       }
+      UnitInfo next;
+      int next_lo = 0, next_hi = 0;
+      read_header(lu + 1, next, next_lo, next_hi);
       mbar_wait(o_full, lu & 1, p.err);
       tc_fence_after();
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
@@ -1160,6 +1171,9 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         p.lse[(long long)ui.head * p.total_q + tq] = lse;
       }
       tc_fence_before();
+      ui = next;
+      klo = next_lo;
+      khi = next_hi;
     }
     if (C::kTmaOut && lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
