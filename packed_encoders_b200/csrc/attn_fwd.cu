@@ -359,6 +359,23 @@ __device__ __forceinline__ uint4 load_gate8(const AttnParams& p, int tok, int he
 __global__ void __launch_bounds__(256) gate_pass_kernel(__nv_bfloat16* out, const __nv_bfloat16* gate, int total_q,
                                                         int heads, int vec_per_row, long long o_tok, long long o_head,
                                                         long long g_tok, long long g_head) {
+#ifdef PE_GATE_GRID
+  // One 16-byte vector of the [token][head][column] output per thread and no loop: the grid
+  // covers the tensor (many small CTAs, like an elementwise kernel).
+  {
+    const long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long n = (long long)total_q * heads * vec_per_row;
+    if (v >= n) return;
+    const int t = (int)(v / (heads * vec_per_row));
+    const int rem = (int)(v - (long long)t * heads * vec_per_row);
+    const int h = rem / vec_per_row, c = (rem - h * vec_per_row) * 8;
+    __nv_bfloat16* op = out + (long long)t * o_tok + (long long)h * o_head + c;
+    const uint4 ov = *reinterpret_cast<const uint4*>(op);
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate + (long long)t * g_tok + (long long)h * g_head + c));
+    *reinterpret_cast<uint4*>(op) = gate8(ov, gv);
+    return;
+  }
+#endif
   const int per_tok = heads * vec_per_row;
   const int step = gridDim.x;
   for (int t = threadIdx.x; t < per_tok; t += blockDim.x) {
@@ -378,7 +395,11 @@ __global__ void __launch_bounds__(256) gate_pass_kernel(__nv_bfloat16* out, cons
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int tk = tok + u * step;
+#ifdef PE_GATE_PLAINST
+        if (tk < total_q) *reinterpret_cast<uint4*>(o_base + (long long)tk * o_tok) = gate8(ov[u], gv[u]);
+#else
         if (tk < total_q) __stcs(reinterpret_cast<uint4*>(o_base + (long long)tk * o_tok), gate8(ov[u], gv[u]));
+#endif
       }
     }
   }
@@ -1650,7 +1671,11 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
     st = pe_b200_attn_run(&ungated, stream);
     if (st != PE_B200_OK) return st;
     const long long slots = (long long)info.sms * info.gate_blocks_per_sm;
+#ifdef PE_GATE_GRID
+    const int grid = (int)(((long long)p->total_q * p->heads * (p->head_dim / 8) + 255) / 256);
+#else
     const int grid = (int)(p->total_q < slots ? p->total_q : slots);
+#endif
     gate_pass_kernel<<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(p->out), static_cast<const __nv_bfloat16*>(p->gate),
                                           p->total_q, p->heads, p->head_dim / 8, p->o_stride_token, p->o_stride_head,
                                           p->g_stride_token, p->g_stride_head);
