@@ -356,53 +356,22 @@ __device__ __forceinline__ uint4 load_gate8(const AttnParams& p, int tok, int he
 // is slower: each thread owns one 16-byte vector (head, 8 columns) of a token row and walks the
 // tokens with a grid stride, four tokens per step so eight loads are in flight; the fused
 // path's roundings (gate8).
+// One 16-byte vector of the [token][head][column] output per thread, in place, and a grid that
+// covers the tensor (no loop): measured 7 % faster than a one-wave persistent grid with four
+// tokens in flight per thread (config 5 shapes, 1.06 vs 1.14 ms).
 __global__ void __launch_bounds__(256) gate_pass_kernel(__nv_bfloat16* out, const __nv_bfloat16* gate, int total_q,
                                                         int heads, int vec_per_row, long long o_tok, long long o_head,
                                                         long long g_tok, long long g_head) {
-#ifdef PE_GATE_GRID
-  // One 16-byte vector of the [token][head][column] output per thread and no loop: the grid
-  // covers the tensor (many small CTAs, like an elementwise kernel).
-  {
-    const long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long long n = (long long)total_q * heads * vec_per_row;
-    if (v >= n) return;
-    const int t = (int)(v / (heads * vec_per_row));
-    const int rem = (int)(v - (long long)t * heads * vec_per_row);
-    const int h = rem / vec_per_row, c = (rem - h * vec_per_row) * 8;
-    __nv_bfloat16* op = out + (long long)t * o_tok + (long long)h * o_head + c;
-    const uint4 ov = *reinterpret_cast<const uint4*>(op);
-    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate + (long long)t * g_tok + (long long)h * g_head + c));
-    *reinterpret_cast<uint4*>(op) = gate8(ov, gv);
-    return;
-  }
-#endif
+  const long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_tok = heads * vec_per_row;
-  const int step = gridDim.x;
-  for (int t = threadIdx.x; t < per_tok; t += blockDim.x) {
-    const int h = t / vec_per_row, c = (t - h * vec_per_row) * 8;
-    __nv_bfloat16* o_base = out + (long long)h * o_head + c;
-    const __nv_bfloat16* g_base = gate + (long long)h * g_head + c;
-    for (int tok = blockIdx.x; tok < total_q; tok += 4 * step) {
-      uint4 ov[4], gv[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int tk = tok + u * step;
-        if (tk < total_q) {
-          ov[u] = *reinterpret_cast<const uint4*>(o_base + (long long)tk * o_tok);
-          gv[u] = __ldg(reinterpret_cast<const uint4*>(g_base + (long long)tk * g_tok));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int tk = tok + u * step;
-#ifdef PE_GATE_PLAINST
-        if (tk < total_q) *reinterpret_cast<uint4*>(o_base + (long long)tk * o_tok) = gate8(ov[u], gv[u]);
-#else
-        if (tk < total_q) __stcs(reinterpret_cast<uint4*>(o_base + (long long)tk * o_tok), gate8(ov[u], gv[u]));
-#endif
-      }
-    }
-  }
+  if (v >= (long long)total_q * per_tok) return;
+  const int t = (int)(v / per_tok);
+  const int rem = (int)(v - (long long)t * per_tok);
+  const int h = rem / vec_per_row, c = (rem - h * vec_per_row) * 8;
+  __nv_bfloat16* op = out + (long long)t * o_tok + (long long)h * o_head + c;
+  const uint4 ov = *reinterpret_cast<const uint4*>(op);
+  const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate + (long long)t * g_tok + (long long)h * g_head + c));
+  *reinterpret_cast<uint4*>(op) = gate8(ov, gv);
 }
 
 // Rotary embedding of q and k (head_dim 64) into contiguous [T, H, 64] / [T, KV, 64] buffers. Work
@@ -1400,7 +1369,6 @@ static bool make_map_panels(CUtensorMap* map, const void* base, long long tokens
 struct DeviceInfo {
   int sms = 0;
   int supported = -1;
-  int gate_blocks_per_sm = 0;  // resident gate_pass_kernel CTAs per SM (one wave, no tail)
 };
 
 // Per-device facts, looked up once per device under a lock (calls may come from several host
@@ -1417,14 +1385,6 @@ static DeviceInfo& device_info(int dev) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     d.sms = sms;
     d.supported = (major == 10 && minor == 0) ? 1 : 0;
-    if (d.supported == 1) {
-      int cur = -1, per_sm = 0;
-      cudaGetDevice(&cur);
-      if (cur == dev && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gate_pass_kernel, 256, 0) == cudaSuccess)
-        d.gate_blocks_per_sm = per_sm;
-      cudaGetLastError();
-    }
-    if (d.gate_blocks_per_sm < 1) d.gate_blocks_per_sm = 4;
   }
   return d;
 }
@@ -1670,12 +1630,9 @@ int pe_b200_attn_run(const PeB200AttnParams* p, void* stream) {
     ungated.gate = nullptr;
     st = pe_b200_attn_run(&ungated, stream);
     if (st != PE_B200_OK) return st;
-    const long long slots = (long long)info.sms * info.gate_blocks_per_sm;
-#ifdef PE_GATE_GRID
-    const int grid = (int)(((long long)p->total_q * p->heads * (p->head_dim / 8) + 255) / 256);
-#else
-    const int grid = (int)(p->total_q < slots ? p->total_q : slots);
-#endif
+    const long long vecs = (long long)p->total_q * p->heads * (p->head_dim / 8);
+    if (vecs > 256LL * 0x7fffffffLL) return PE_B200_ERR_SHAPE;
+    const int grid = (int)((vecs + 255) / 256);
     gate_pass_kernel<<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(p->out), static_cast<const __nv_bfloat16*>(p->gate),
                                           p->total_q, p->heads, p->head_dim / 8, p->o_stride_token, p->o_stride_head,
                                           p->g_stride_token, p->g_stride_head);
