@@ -38,8 +38,8 @@ sys.path.insert(0, str(ROOT))
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one full-size attn_fwd_kernel launch (config 3
 # global layer, all 512 documents), from a one-pass ncu capture of
-# `python bench.py --case config3-global --iters 2`: 3.668 GB read + 0.899 GB written.
-NCU_TRAFFIC_GLOBAL = 3.668e9 + 0.899e9
+# `python bench.py --case config3-global --iters 2`: 3.698 GB read + 0.899 GB written.
+NCU_TRAFFIC_GLOBAL = 3.698e9 + 0.899e9
 
 
 def _env_int(name, default):
