@@ -528,10 +528,16 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           const int col0 = cc * 32 + 2 * j;
           const bool ok0 = (unsigned)(col0 - c_lo) < (unsigned)(c_hi - c_lo);
           const bool ok1 = (unsigned)(col0 + 1 - c_lo) < (unsigned)(c_hi - c_lo);
-          const float p0 = ok0 ? ex2(fmaf(__uint_as_float(s[2 * j]), c2, -lse2)) : 0.f;
-          const float p1 = ok1 ? ex2(fmaf(__uint_as_float(s[2 * j + 1]), c2, -lse2)) : 0.f;
+          // packed f32x2 arithmetic: the same roundings as the scalar form, half the instructions
+          const float2 x = ffma2(make_float2(__uint_as_float(s[2 * j]), __uint_as_float(s[2 * j + 1])),
+                                 make_float2(c2, c2), make_float2(-lse2, -lse2));
+          const float p0 = ok0 ? ex2(x.x) : 0.f;
+          const float p1 = ok1 ? ex2(x.y) : 0.f;
           pk[j] = pack_bf16x2(p0, p1);
-          dk16[j] = pack_bf16x2(p0 * (__uint_as_float(dp[2 * j]) - dsum), p1 * (__uint_as_float(dp[2 * j + 1]) - dsum));
+          const float2 d = fadd2(make_float2(__uint_as_float(dp[2 * j]), __uint_as_float(dp[2 * j + 1])),
+                                 make_float2(-dsum, -dsum));
+          const float2 g = fmul2(make_float2(p0, p1), d);
+          dk16[j] = pack_bf16x2(g.x, g.y);
         }
         // chunks 4*h2 .. +3 of panel `half`, swizzled by the row
 #pragma unroll
