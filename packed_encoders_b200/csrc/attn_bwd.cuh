@@ -572,6 +572,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     if (pend) finish(pi, pqt, pnq, phead, plast, pkb0, pnk);
   }
 
+  drain_after_timeout(p.err);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

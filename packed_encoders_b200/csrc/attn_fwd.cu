@@ -1168,6 +1168,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
     if (C::kTmaOut && lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
   }
 
+  drain_after_timeout(p.err);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

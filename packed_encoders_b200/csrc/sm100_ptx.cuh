@@ -87,6 +87,15 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // phase completed, so a lost arrival yields wrong numbers plus an error flag, never a hang.
 constexpr long long kWaitBudgetCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
+// After a wait of this launch gave up (the error word is set), the roles went on without their
+// barriers, so copies and MMAs of this CTA may still be in flight: give them ~200 us to land before
+// the CTA frees its TMEM and exits. Called by every thread before the final barrier; free when no
+// wait gave up.
+__device__ __forceinline__ void drain_after_timeout(const int* err) {
+  if (err && *reinterpret_cast<const volatile int*>(err) != 0)
+    for (int k = 0; k < 200; ++k) __nanosleep(1000);
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_test_wait(bar, parity)) return true;
   if (mbar_try_wait(bar, parity)) return true;
