@@ -889,6 +889,135 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       __syncwarp();
       if (lane == 0) mbar_arrive(&row_empty[qb]);
     };
+    // Epilogue of unit `eu` (its running max m_e and sum l_e; o_full phase of unit elu): O / l -> bf16
+    // rows, LSE in natural log.
+    auto epilogue = [&](const UnitInfo& eu, float m_e, float l_e, int elu) {
+      const bool row_valid = r < eu.nq;
+      const int tq = eu.q_row0 + r;
+      const float inv = l_e > 0.f ? 1.f / l_e : 0.f;
+      // Gated calls (rows stored by their own thread): the first gate chunk is in flight while
+      // the last P.V completes.
+      constexpr int kGateChunk = C::CPS == 1 ? 8 : 4;  // uint4 per 32*kEpi columns
+      uint4 g_next[(C::kGate && !C::kStageOut) ? kGateChunk : 1];
+      if constexpr (C::kGate && !C::kStageOut) {
+        if (row_valid && tq < p.total_q) {
+#pragma unroll
+          for (int j = 0; j < kGateChunk; ++j) g_next[j] = load_gate8(p, tq, eu.head, j * 8);
+        }
+      }
+      mbar_wait(o_full, elu & 1, p.err);
+      tc_fence_after();
+      const bool store = row_valid && tq >= 0 && tq < p.total_q;
+      __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)eu.head * p.o_head;
+      if constexpr (C::kTmaOut) {
+        // The warp's 32 rows go to its 4 KB stage, then leave with one TMA store; a previous
+        // store from the stage must have finished reading it first.
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+      }
+      const bool tma_rows = C::kTmaOut && quarter * 32 + 32 <= eu.nq && eu.q_row0 + quarter * 32 + 32 <= p.total_q;
+      if (tma_rows) {
+        uint8_t* stage = smem + C::stage_off(quarter);
+        uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
+        tmem_ld32(o_addr, oo[0]);
+        tmem_ld32(o_addr + 32, oo[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t* o = oo[hh];
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 val = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            if constexpr (C::kGate) val = gate8(val, load_gate8(p, tq, eu.head, hh * 32 + c * 8));
+            *reinterpret_cast<uint4*>(stage + lane * 128 + (((hh * 4 + c) ^ (lane & 7)) * 16)) = val;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (kStreamOut) tma_store_3d_hint(&tm_o, stage, 0, eu.head, eu.q_row0 + quarter * 32, l2_policy_evict_first());
+          else tma_store_3d(&tm_o, stage, 0, eu.head, eu.q_row0 + quarter * 32);
+          bulk_commit_group();
+        }
+      } else if constexpr (C::kStageOut) {
+        // 64 output columns per thread, in two 32-column halves: each half of all 32 rows of the
+        // warp goes through a 2 KB buffer (16-byte chunk c of row r at r*4 + (c ^ (r/2 % 4)),
+        // conflict-free both ways) and leaves as 64-byte row segments, 8 rows per instruction.
+        uint4* stage = reinterpret_cast<uint4*>(smem + C::stage_off(quarter));
+        uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
+        tmem_ld32(o_addr, oo[0]);
+        tmem_ld32(o_addr + 32, oo[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t* o = oo[hh];
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            stage[lane * 4 + (c ^ ((lane >> 1) & 3))] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int row = k * 8 + (lane >> 2), c = lane & 3;
+            uint4 val = stage[row * 4 + (c ^ ((row >> 1) & 3))];
+            const int tr = quarter * 32 + row;  // tile row
+            const int tok = eu.q_row0 + tr;
+            if (tr < eu.nq && tok < p.total_q) {
+              if constexpr (C::kGate) val = gate8(val, load_gate8(p, tok, eu.head, hh * 32 + c * 8));
+              store_out(reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)eu.head * p.o_head +
+                                                 hh * 32 + c * 8),
+                        val);
+            }
+          }
+          __syncwarp();
+        }
+      } else {
+        constexpr int kEpi = C::CPS == 1 ? 2 : 1;  // 32-column chunks per TMEM load
+        // Gated calls: the gate of the next 32*kEpi columns is loaded while this chunk is finished.
+        static_assert(!C::kGate || kGateChunk == kEpi * 4, "gate chunk");
+#pragma unroll
+        for (int cc = 0; cc < kOCols / 32; cc += kEpi) {
+          uint32_t o[kEpi * 32];
+          tmem_ld_chunks<kEpi>(o_addr + cc * 32, o);
+          tmem_wait_ld();
+          uint32_t pk[kEpi * 16];
+#pragma unroll
+          for (int j = 0; j < kEpi * 16; ++j)
+            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+          if (store) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+            uint4 g_cur[C::kGate ? kEpi * 4 : 1];
+            if constexpr (C::kGate) {
+#pragma unroll
+              for (int j = 0; j < kEpi * 4; ++j) g_cur[j] = g_next[j];
+              if (cc + kEpi < kOCols / 32) {
+#pragma unroll
+                for (int j = 0; j < kEpi * 4; ++j)
+                  g_next[j] = load_gate8(p, tq, eu.head, (cc + kEpi) * 32 + j * 8);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < kEpi * 4; ++j) {
+              uint4 val = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+              if constexpr (C::kGate) val = gate8(val, g_cur[j]);
+              store_out(dst + j, val);
+            }
+          }
+        }
+      }
+      if (store && p.lse != nullptr) {
+        const float lse = l_e > 0.f ? (m_e + __log2f(l_e)) * 0.69314718055994531f : NEG_INF;
+        p.lse[(long long)eu.head * p.total_q + tq] = lse;
+      }
+      tc_fence_before();
+    };
     read_header(0, ui, klo, khi);
     for (int lu = 0;; ++lu) {
       if (ui.n_kv < 0) break;
@@ -1034,133 +1163,10 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[sb]);
       }
-      // Epilogue: O / l -> bf16 rows, LSE in natural log.
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      // Gated calls (rows stored by their own thread): the first gate chunk is in flight while
-      // the last P.V completes.
-      constexpr int kGateChunk = C::CPS == 1 ? 8 : 4;  // uint4 per 32*kEpi columns
-      uint4 g_next[(C::kGate && !C::kStageOut) ? kGateChunk : 1];
-      if constexpr (C::kGate && !C::kStageOut) {
-        if (row_valid && tq < p.total_q) {
-#pragma unroll
-          for (int j = 0; j < kGateChunk; ++j) g_next[j] = load_gate8(p, tq, ui.head, j * 8);
-        }
-      }
       UnitInfo next;
       int next_lo = 0, next_hi = 0;
       read_header(lu + 1, next, next_lo, next_hi);
-      mbar_wait(o_full, lu & 1, p.err);
-      tc_fence_after();
-      const bool store = row_valid && tq >= 0 && tq < p.total_q;
-      __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)ui.head * p.o_head;
-      if constexpr (C::kTmaOut) {
-        // The warp's 32 rows go to its 4 KB stage, then leave with one TMA store; a previous
-        // store from the stage must have finished reading it first.
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-      }
-      const bool tma_rows = C::kTmaOut && quarter * 32 + 32 <= ui.nq && ui.q_row0 + quarter * 32 + 32 <= p.total_q;
-      if (tma_rows) {
-        uint8_t* stage = smem + C::stage_off(quarter);
-        uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
-        tmem_ld32(o_addr, oo[0]);
-        tmem_ld32(o_addr + 32, oo[1]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t* o = oo[hh];
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint4 val = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-            if constexpr (C::kGate) val = gate8(val, load_gate8(p, tq, ui.head, hh * 32 + c * 8));
-            *reinterpret_cast<uint4*>(stage + lane * 128 + (((hh * 4 + c) ^ (lane & 7)) * 16)) = val;
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (kStreamOut) tma_store_3d_hint(&tm_o, stage, 0, ui.head, ui.q_row0 + quarter * 32, l2_policy_evict_first());
-          else tma_store_3d(&tm_o, stage, 0, ui.head, ui.q_row0 + quarter * 32);
-          bulk_commit_group();
-        }
-      } else if constexpr (C::kStageOut) {
-        // 64 output columns per thread, in two 32-column halves: each half of all 32 rows of the
-        // warp goes through a 2 KB buffer (16-byte chunk c of row r at r*4 + (c ^ (r/2 % 4)),
-        // conflict-free both ways) and leaves as 64-byte row segments, 8 rows per instruction.
-        uint4* stage = reinterpret_cast<uint4*>(smem + C::stage_off(quarter));
-        uint32_t oo[2][32];  // both 32-column halves of O, one TMEM wait
-        tmem_ld32(o_addr, oo[0]);
-        tmem_ld32(o_addr + 32, oo[1]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t* o = oo[hh];
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            stage[lane * 4 + (c ^ ((lane >> 1) & 3))] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int row = k * 8 + (lane >> 2), c = lane & 3;
-            uint4 val = stage[row * 4 + (c ^ ((row >> 1) & 3))];
-            const int tr = quarter * 32 + row;  // tile row
-            const int tok = ui.q_row0 + tr;
-            if (tr < ui.nq && tok < p.total_q) {
-              if constexpr (C::kGate) val = gate8(val, load_gate8(p, tok, ui.head, hh * 32 + c * 8));
-              store_out(reinterpret_cast<uint4*>(p.out + (long long)tok * p.o_tok + (long long)ui.head * p.o_head +
-                                                 hh * 32 + c * 8),
-                        val);
-            }
-          }
-          __syncwarp();
-        }
-      } else {
-        constexpr int kEpi = C::CPS == 1 ? 2 : 1;  // 32-column chunks per TMEM load
-        // Gated calls: the gate of the next 32*kEpi columns is loaded while this chunk is finished.
-        static_assert(!C::kGate || kGateChunk == kEpi * 4, "gate chunk");
-#pragma unroll
-        for (int cc = 0; cc < kOCols / 32; cc += kEpi) {
-          uint32_t o[kEpi * 32];
-          tmem_ld_chunks<kEpi>(o_addr + cc * 32, o);
-          tmem_wait_ld();
-          uint32_t pk[kEpi * 16];
-#pragma unroll
-          for (int j = 0; j < kEpi * 16; ++j)
-            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
-          if (store) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
-            uint4 g_cur[C::kGate ? kEpi * 4 : 1];
-            if constexpr (C::kGate) {
-#pragma unroll
-              for (int j = 0; j < kEpi * 4; ++j) g_cur[j] = g_next[j];
-              if (cc + kEpi < kOCols / 32) {
-#pragma unroll
-                for (int j = 0; j < kEpi * 4; ++j)
-                  g_next[j] = load_gate8(p, tq, ui.head, (cc + kEpi) * 32 + j * 8);
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < kEpi * 4; ++j) {
-              uint4 val = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-              if constexpr (C::kGate) val = gate8(val, g_cur[j]);
-              store_out(dst + j, val);
-            }
-          }
-        }
-      }
-      if (store && p.lse != nullptr) {
-        const float lse = l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994531f : NEG_INF;
-        p.lse[(long long)ui.head * p.total_q + tq] = lse;
-      }
-      tc_fence_before();
+      epilogue(ui, m_run, l_run, lu);
       ui = next;
       klo = next_lo;
       khi = next_hi;
