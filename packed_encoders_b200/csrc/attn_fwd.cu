@@ -208,7 +208,10 @@ __global__ void __launch_bounds__(kBuilderThreads) schedule_kernel(SchedParams p
   __shared__ int bad;
   const int tid = threadIdx.x;
   for (int b = tid; b < kCostBuckets; b += blockDim.x) hist[b] = 0;
-  if (tid == 0) bad = 0;
+  if (tid == 0) {
+    bad = 0;
+    p.header->error = 0;  // the header is this thread's alone; n_items is written at the end
+  }
   __syncthreads();
   for (int s = tid; s < p.n_seq; s += blockDim.x) {
     int q0 = p.cu_q[s], q1 = p.cu_q[s + 1], k0 = p.cu_k[s], k1 = p.cu_k[s + 1];
@@ -1582,8 +1585,9 @@ int pe_b200_build_schedule(const PeB200AttnParams* p, void* stream) {
   if (device_info(dev).supported != 1) return PE_B200_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   WsHeader* header = static_cast<WsHeader*>(p->workspace);
-  clear_header_kernel<<<1, 1, 0, s>>>(header);
-  if (p->n_seq > 0 && p->total_q > 0) {
+  if (p->n_seq == 0 || p->total_q == 0) {
+    clear_header_kernel<<<1, 1, 0, s>>>(header);  // an empty schedule
+  } else {
     SchedParams sp;
     sp.cu_q = p->cu_seqlens_q;
     sp.cu_k = p->cu_seqlens_k;

@@ -17,6 +17,7 @@ Reference interfaces mirrored (packed-encoders 0.3.0):
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
@@ -81,6 +82,14 @@ def _count(n: int) -> None:
     LAUNCHES["kernels"] += n
 
 
+def _extra_passes(rope, gate) -> int:
+    """Kernels a call launches besides the schedule build and the attention kernel: the RoPE pass,
+    and the output-gate pass unless the gate is fused into the epilogue (PE_B200_GATE=fused, which
+    the library reads once per process)."""
+    gate_pass = gate is not None and os.environ.get("PE_B200_GATE") != "fused"
+    return (1 if rope is not None else 0) + (1 if gate_pass else 0)
+
+
 class AttentionPlan:
     """A device tile schedule built once for one set of segment boundaries and one attention
     kind (window / causal / head_dim), reusable by every layer of a forward that shares them
@@ -132,7 +141,7 @@ class AttentionPlan:
             stream = torch.cuda.current_stream(device)
             _lib.check(so.pe_b200_build_schedule(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)),
                        "pe_b200_build_schedule")
-        _count(2)
+        _count(1)
 
     def error_word(self) -> int:
         """Synchronising read of the device error word of the last build / run on this plan."""
@@ -258,7 +267,7 @@ def packed_attention(
             params.workspace_bytes = plan.workspace.numel()
             _lib.check(so.pe_b200_attn_run(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)),
                        "pe_b200_attn_run")
-            _count(1)
+            _count(1 + _extra_passes(rope, gate))
         else:
             nbytes = ctypes.c_size_t(0)
             _lib.check(so.pe_b200_attn_workspace_size(ctypes.byref(params), ctypes.byref(nbytes)), "workspace size")
@@ -267,7 +276,7 @@ def packed_attention(
             params.workspace_bytes = ws.numel()
             _lib.check(so.pe_b200_attn_fwd(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)),
                        "pe_b200_attn_fwd")
-            _count(3)
+            _count(2 + _extra_passes(rope, gate))  # schedule build + attention
     return (out, lse) if return_lse else out
 
 
@@ -312,7 +321,7 @@ def packed_attention_backward(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device)
         _lib.check(so.pe_b200_attn_bwd(ctypes.byref(params), ctypes.c_void_p(stream.cuda_stream)), "pe_b200_attn_bwd")
-    _count(5)
+    _count(4)  # per-row prep, schedule build, backward, dq conversion
     return dq, dk, dv  # the workspace returns to torch's stream-ordered allocator
 
 
