@@ -1024,8 +1024,6 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
     read_header(0, ui, klo, khi);
     for (int lu = 0;; ++lu) {
       if (ui.n_kv < 0) break;
-      const bool row_valid = r < ui.nq;
-      const int tq = ui.q_row0 + r;
       float m_run = NEG_INF, l_run = 0.f;
       for (int t = 0; t < ui.n_kv; ++t, ++i) {
         const int sb = (int)(i % C::NS);
