@@ -137,3 +137,61 @@ def test_autograd_through_rectangular_flash_attention():
     _check("rectangular dq", g[:, :, 0].reshape(b * s, heads, 64), rdq)
     _check("rectangular dk", g[:, :, 1].reshape(b * s, heads, 64), rdk)
     _check("rectangular dv", g[:, :, 2].reshape(b * s, heads, 64), rdv)
+
+
+def _sdpa_grads_fp32(q, k, v, cu, dout, scale, window):
+    """dq, dk, dv of fp32 attention per sequence on the GPU (torch SDPA; a band mask for windows)."""
+    import torch.nn.functional as F
+
+    qf, kf, vf = (t.detach().float().requires_grad_() for t in (q, k, v))
+    outs = []
+    bounds = cu.tolist()
+    for a, b in zip(bounds, bounds[1:]):
+        n = b - a
+        if n == 0:
+            continue
+        qs, ks, vs = (t[a:b].transpose(0, 1).unsqueeze(0) for t in (qf, kf, vf))  # [1, H, n, D]
+        mask = None
+        if window != (-1, -1):
+            i = torch.arange(n, device=q.device)
+            d = i[:, None] - i[None, :]
+            mask = (d <= window[0]) & (-d <= window[1])
+        o = F.scaled_dot_product_attention(qs, ks, vs, attn_mask=mask, scale=scale)
+        outs.append(o.squeeze(0).transpose(0, 1))
+    torch.cat(outs).backward(dout.float())
+    return qf.grad, kf.grad, vf.grad
+
+
+@pytest.mark.parametrize("kind", ["global", "local"])
+def test_backward_config3_documents_vs_fp32_and_fa2(kind):
+    """Config 3 documents (log-normal lengths up to 8,192 tokens, 16 heads x 64): dq, dk, dv against
+    fp32 attention on the GPU, with FlashAttention-2's varlen backward (the reference's compiled
+    path) on the same inputs as the yardstick: our error may not exceed 1.25x FA2's plus a bf16
+    quantum, and stays within 2e-2 of the largest reference value."""
+    fa = pytest.importorskip("flash_attn")
+    import packed_encoders_b200 as pe
+    from packed_encoders_b200 import workloads as wl
+
+    lengths = list(wl.config3_lengths())
+    lengths = lengths[:48] if kind == "global" else [n for n in lengths if n <= 2048][:48]
+    window = (-1, -1) if kind == "global" else (64, 64)
+    heads = 16
+    q, k, v, cu = packed_inputs(lengths, heads, 64, seed=61, device="cuda")
+    dout = torch.randn(q.shape, device="cuda", generator=torch.Generator("cuda").manual_seed(62)).to(torch.bfloat16)
+    scale = 0.125
+    out, lse = pe.packed_attention(q, k, v, cu, max(lengths), scale=scale, window=window, return_lse=True)
+    ours = pe.packed_attention_backward(dout, q, k, v, out, lse, cu, max(lengths), scale=scale, window=window)
+    qg, kg, vg = (t.detach().clone().requires_grad_() for t in (q, k, v))
+    o = fa.flash_attn_varlen_func(qg, kg, vg, cu, cu, max(lengths), max(lengths), softmax_scale=scale,
+                                  window_size=window)
+    theirs = torch.autograd.grad(o, (qg, kg, vg), dout)
+    ref = _sdpa_grads_fp32(q, k, v, cu, dout, scale, window)
+    torch.cuda.synchronize()
+    for name, a, b, r in zip(("dq", "dk", "dv"), ours, theirs, ref):
+        e_ours = (a.float() - r).abs().max().item()
+        e_fa2 = (b.float() - r).abs().max().item()
+        top = r.abs().max().item()
+        print(f"PARITY backward {kind} {name} ({len(lengths)} docs, {sum(lengths)} tokens): max_abs={e_ours:.5f} "
+              f"fa2_max_abs={e_fa2:.5f} ref_max={top:.4f}")
+        assert e_ours <= 1.25 * e_fa2 + 2 ** -8 * top, f"{name}: {e_ours:.4g} vs FA2 {e_fa2:.4g}"
+        assert e_ours <= 2e-2 * top, f"{name}: {e_ours:.4g} > 2e-2 x {top:.4g}"
