@@ -97,6 +97,11 @@ struct AttnParams {
   long long g_tok;
   long long g_head;
   int kv_major;  // unit order (unit_coords)
+  // q, k, v as the tensor maps read them; only the non-finite row rewrite reads them through these.
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  long long q_tok, q_head, k_tok, k_head, v_tok, v_head;
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -588,6 +593,65 @@ __device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[N *
   for (int c = 0; c < N; ++c) tmem_ld32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
 }
 
+// Non-finite inputs. A key tile's P.V multiplies every key row the tile holds, including rows of
+// neighbouring sequences and rows past a segment's end, whose P is 0; 0 x Inf is NaN, so one
+// non-finite V row would spread to the other sequences of its tile. The epilogue therefore sums
+// a row's O values as they leave TMEM (one NaN or Inf makes the sum non-finite) and rewrites a
+// row whose sum is non-finite from its own allowed keys [klo, khi) alone, in fp32 with the tile
+// loop's max and sum: a non-finite value then reaches exactly the queries that attend to its key,
+// as in a per-sequence computation. Finite inputs never take the rewrite; the check is one
+// packed-add tree per row (measured: +0.6 % on a long-document global layer, +3 % on a windowed
+// one, +10 % on a batch of very short sequences, where the epilogue is a large share of a unit).
+__device__ __forceinline__ float2 chunk_sum32(const uint32_t* o, float2 acc) {
+  float2 b = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    acc = fadd2(acc, make_float2(__uint_as_float(o[j]), __uint_as_float(o[j + 1])));
+    b = fadd2(b, make_float2(__uint_as_float(o[j + 2]), __uint_as_float(o[j + 3])));
+  }
+  return fadd2(acc, b);
+}
+
+// o[0 .. 32) = sum_j exp2(c2 * (q . k_j) - m) * v_j[col0 .. col0 + 32) over keys [klo, khi), in
+// fp32 from bf16 rows (qrow: the query row; kbase / vbase: the row of token 0 at the unit's KV
+// head). Accumulates in the chunk's own registers.
+template <int D>
+__device__ __forceinline__ void recompute_chunk(uint32_t* o, const __nv_bfloat16* qrow, const __nv_bfloat16* kbase,
+                                                const __nv_bfloat16* vbase, long long k_tok, long long v_tok,
+                                                float c2, float m, int klo, int khi, int col0) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) o[j] = 0u;
+#pragma unroll 1
+  for (int key = klo; key < khi; ++key) {
+    const uint4* krow = reinterpret_cast<const uint4*>(kbase + (long long)key * k_tok);
+    float s = 0.f;
+#pragma unroll 1
+    for (int d = 0; d < D / 8; ++d) {
+      const uint4 a = reinterpret_cast<const uint4*>(qrow)[d];
+      const uint4 b = krow[d];
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s = fmaf(__uint_as_float(aw[e] << 16), __uint_as_float(bw[e] << 16), s);
+        s = fmaf(__uint_as_float(aw[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u), s);
+      }
+    }
+    const float pj = ex2(fmaf(s, c2, -m));
+    const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (long long)key * v_tok + col0);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 w = vrow[c];
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o[c * 8 + 2 * e] = __float_as_uint(fmaf(pj, __uint_as_float(ww[e] << 16), __uint_as_float(o[c * 8 + 2 * e])));
+        o[c * 8 + 2 * e + 1] =
+            __float_as_uint(fmaf(pj, __uint_as_float(ww[e] & 0xffff0000u), __uint_as_float(o[c * 8 + 2 * e + 1])));
+      }
+    }
+  }
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -911,6 +975,9 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       mbar_wait(o_full, elu & 1, p.err);
       tc_fence_after();
       const bool store = row_valid && tq >= 0 && tq < p.total_q;
+      // Sum of the row's O values as they leave TMEM: non-finite iff some value is (or the sum of
+      // huge finite values overflows, which only costs a recomputation).
+      float2 o_sum = make_float2(0.f, 0.f);
       __nv_bfloat16* orow = p.out + (long long)tq * p.o_tok + (long long)eu.head * p.o_head;
       if constexpr (C::kTmaOut) {
         // The warp's 32 rows go to its 4 KB stage, then leave with one TMA store; a previous
@@ -925,6 +992,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         tmem_ld32(o_addr, oo[0]);
         tmem_ld32(o_addr + 32, oo[1]);
         tmem_wait_ld();
+        o_sum = chunk_sum32(oo[1], chunk_sum32(oo[0], o_sum));
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const uint32_t* o = oo[hh];
@@ -955,6 +1023,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
         tmem_ld32(o_addr, oo[0]);
         tmem_ld32(o_addr + 32, oo[1]);
         tmem_wait_ld();
+        o_sum = chunk_sum32(oo[1], chunk_sum32(oo[0], o_sum));
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const uint32_t* o = oo[hh];
@@ -990,6 +1059,8 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           uint32_t o[kEpi * 32];
           tmem_ld_chunks<kEpi>(o_addr + cc * 32, o);
           tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < kEpi; ++e) o_sum = chunk_sum32(&o[e * 32], o_sum);
           uint32_t pk[kEpi * 16];
 #pragma unroll
           for (int j = 0; j < kEpi * 16; ++j)
@@ -1018,6 +1089,37 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       if (store && p.lse != nullptr) {
         const float lse = l_e > 0.f ? (m_e + __log2f(l_e)) * 0.69314718055994531f : NEG_INF;
         p.lse[(long long)eu.head * p.total_q + tq] = lse;
+      }
+      // Rows with a non-finite output are rewritten from their own keys (recompute_chunk), after
+      // the warp's bulk output store has landed.
+      const bool nonfinite = store && (__float_as_uint(o_sum.x + o_sum.y) & 0x7f800000u) == 0x7f800000u;
+      if (__any_sync(0xffffffffu, nonfinite)) {
+        if constexpr (C::kTmaOut) {
+          if (lane == 0) {
+            bulk_wait_all();
+            fence_proxy_async_global();
+          }
+          __syncwarp();
+        }
+        if (nonfinite) {
+          const int kvh = eu.head / p.group;
+          const __nv_bfloat16* qrow = p.q + (long long)tq * p.q_tok + (long long)eu.head * p.q_head;
+#pragma unroll 1
+          for (int cc = 0; cc < kOCols / 32; ++cc) {
+            uint32_t o[32];
+            recompute_chunk<C::D>(o, qrow, p.k + (long long)kvh * p.k_head, p.v + (long long)kvh * p.v_head, p.k_tok,
+                                  p.v_tok, c2, m_e == NEG_INF ? 0.f : m_e, klo, khi, cc * 32);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 val = make_uint4(pack_bf16x2(__uint_as_float(o[8 * j]) * inv, __uint_as_float(o[8 * j + 1]) * inv),
+                                     pack_bf16x2(__uint_as_float(o[8 * j + 2]) * inv, __uint_as_float(o[8 * j + 3]) * inv),
+                                     pack_bf16x2(__uint_as_float(o[8 * j + 4]) * inv, __uint_as_float(o[8 * j + 5]) * inv),
+                                     pack_bf16x2(__uint_as_float(o[8 * j + 6]) * inv, __uint_as_float(o[8 * j + 7]) * inv));
+              if constexpr (C::kGate) val = gate8(val, load_gate8(p, tq, eu.head, cc * 32 + j * 8));
+              *reinterpret_cast<uint4*>(orow + cc * 32 + j * 8) = val;
+            }
+          }
+        }
       }
       tc_fence_before();
     };
@@ -1528,6 +1630,15 @@ static int launch_attention(const PeB200AttnParams* p, cudaStream_t stream, int 
   ap.g_tok = p->g_stride_token;
   ap.g_head = p->g_stride_head;
   ap.kv_major = kv_major ? 1 : 0;
+  ap.q = static_cast<const __nv_bfloat16*>(p->q);
+  ap.k = static_cast<const __nv_bfloat16*>(p->k);
+  ap.v = static_cast<const __nv_bfloat16*>(p->v);
+  ap.q_tok = p->q_stride_token;
+  ap.q_head = p->q_stride_head;
+  ap.k_tok = p->k_stride_token;
+  ap.k_head = p->k_stride_head;
+  ap.v_tok = p->v_stride_token;
+  ap.v_head = p->v_stride_head;
   const long long units = item_capacity(p) * p->heads;
   const long long slots = (long long)sms * C::CPS;
   const int grid = (int)(units < slots ? units : slots);
