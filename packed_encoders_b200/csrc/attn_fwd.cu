@@ -962,6 +962,7 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
       const bool row_valid = r < eu.nq;
       const int tq = eu.q_row0 + r;
       const float inv = l_e > 0.f ? 1.f / l_e : 0.f;
+      const float2 inv2 = make_float2(inv, inv);  // O / l in packed pairs (same rounding as scalar)
       // Gated calls (rows stored by their own thread): the first gate chunk is in flight while
       // the last P.V completes.
       constexpr int kGateChunk = C::CPS == 1 ? 8 : 4;  // uint4 per 32*kEpi columns
@@ -999,7 +1000,10 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+            {
+              const float2 y = fmul2(make_float2(__uint_as_float(o[2 * j]), __uint_as_float(o[2 * j + 1])), inv2);
+              pk[j] = pack_bf16x2(y.x, y.y);
+            }
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint4 val = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
@@ -1030,7 +1034,10 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+            {
+              const float2 y = fmul2(make_float2(__uint_as_float(o[2 * j]), __uint_as_float(o[2 * j + 1])), inv2);
+              pk[j] = pack_bf16x2(y.x, y.y);
+            }
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             stage[lane * 4 + (c ^ ((lane >> 1) & 3))] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
@@ -1064,7 +1071,10 @@ __global__ void __launch_bounds__(C::kThreads) __maxnreg__(C::kMaxRegs)
           uint32_t pk[kEpi * 16];
 #pragma unroll
           for (int j = 0; j < kEpi * 16; ++j)
-            pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+            {
+              const float2 y = fmul2(make_float2(__uint_as_float(o[2 * j]), __uint_as_float(o[2 * j + 1])), inv2);
+              pk[j] = pack_bf16x2(y.x, y.y);
+            }
           if (store) {
             uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
             uint4 g_cur[C::kGate ? kEpi * 4 : 1];
