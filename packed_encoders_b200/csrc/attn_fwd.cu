@@ -600,8 +600,9 @@ __device__ __forceinline__ void tmem_ld_chunks(uint32_t taddr, uint32_t (&r)[N *
 // row whose sum is non-finite from its own allowed keys [klo, khi) alone, in fp32 with the tile
 // loop's max and sum: a non-finite value then reaches exactly the queries that attend to its key,
 // as in a per-sequence computation. Finite inputs never take the rewrite; the check is one
-// packed-add tree per row (measured: +0.6 % on a long-document global layer, +3 % on a windowed
-// one, +10 % on a batch of very short sequences, where the epilogue is a large share of a unit).
+// packed-add tree per row (measured with the packed O / l scaling: +0.6 % on a long-document
+// global layer, +1.6 % on a windowed one, +7 % on a batch of very short sequences, where the
+// epilogue is a large share of a unit).
 __device__ __forceinline__ float2 chunk_sum32(const uint32_t* o, float2 acc) {
   float2 b = make_float2(0.f, 0.f);
 #pragma unroll
